@@ -1,0 +1,561 @@
+"""Benchmark of the sm_100a operator library on BASELINE.json's workloads.
+
+Headline (one JSON line on rank 0): the large sharded Llama-style MLP block of
+BASELINE config 5 -- bf16 RMSNorm of x[16384, 4096] feeding the packed
+GEMM+SwiGLU (M=16384, K=4096, N=14336, W[28672, 4096]) -- as GEMM+SwiGLU
+TFLOP/s for the whole job.  One step = RMSNorm over all rows (each rank needs
+the full normalised X for its N slice) + the N-sharded GEMM+SwiGLU with bf16
+output, all inputs resident in HBM (X 134 MB and W 235 MB exceed the 126 MB
+L2, so no flush between steps is needed).  Scaling is strong: the total work
+is fixed and rank r of N owns output columns [r*N/g, (r+1)*N/g).
+
+Extra keys: ``e2e`` (the same metric through the public API with the X copy
+from pinned host memory and the output shard copied back inside every step),
+``roofline`` (the GEMM kernel against the measured sustained bf16 peak),
+``cpu_baseline`` (the CPU oracle on a row sample, rank 0 at N=1), ``clocks``
+(nvidia-smi sampled during the timed region), ``gpu_launches`` and ``ops``
+(every other BASELINE config: per-op device time, GB/s or TFLOP/s and the
+fraction of the measured peak; the large RMSNorm and the 2^30 reduction are
+measured sharded at every N).
+
+``--impl reference`` times the reference's CPU path (the CPU oracle) on a
+bounded row sample of the same workload, on rank 0 only.
+
+Launch: python bench.py [--gpus N --steps K --warmup W]; for N > 1 under
+torch.distributed.run with one process per GPU (NCCL).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "cuda-operator-lab_b200"))
+sys.path.insert(0, str(ROOT))
+
+M, K, N = 16384, 4096, 14336
+EPS = 1e-6
+SEED = 20261201
+GEMM_FLOPS = 2 * M * K * 2 * N  # 3,848,290,697,216 per step (whole job)
+REDUCTION_N = 1 << 30
+METRIC = ("GEMM+SwiGLU TFLOP/s, Llama MLP block (RMSNorm bf16 -> packed GEMM+SwiGLU bf16, "
+          "M=16384 K=4096 N=14336)")
+
+
+def peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]),
+                "bf16_tflops_sustained": float(data.get("bf16_tflops_sustained",
+                                                        data["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def committed_traffic() -> dict:
+    path = ROOT / "profiles" / "traffic.json"
+    return json.loads(path.read_text()) if path.is_file() else {}
+
+
+# ---------------------------------------------------------------- distributed
+
+
+class Dist:
+    def __init__(self) -> None:
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.enabled = self.world > 1
+        if self.enabled:
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local_rank)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local_rank))
+            self.dist = dist
+        elif torch.cuda.is_available():
+            torch.cuda.set_device(0)
+
+    def barrier(self) -> None:
+        if self.enabled:
+            self.dist.barrier()
+        torch.cuda.synchronize()
+
+    def max(self, value: float) -> float:
+        if not self.enabled:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self) -> None:
+        if self.enabled:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: list[int]) -> None:
+        self.gpus = gpus
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.15)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc) -> None:
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx = int(parts[0])
+            except ValueError:
+                continue
+            if idx in self.gpus:
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+
+        power = [num(r[3]) for r in rows if num(r[3]) is not None]
+        loaded = [r for r in rows if num(r[3]) is not None and num(r[3]) > 0.5 * max(power)] or rows
+        clocks = [num(r[1]) for r in loaded if num(r[1]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i in range(4)
+                          if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(clocks) if clocks else None,
+                "sm_max_mhz": max(num(r[2]) for r in rows if num(r[2]) is not None),
+                "reasons": reasons, "samples": len(loaded),
+                "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------- inputs
+
+
+def make_inputs(d: Dist, device: torch.device) -> dict:
+    """Seeded synthetic inputs of BASELINE config 5 (same X on every rank;
+    rank r keeps gate rows and up rows [r*N/g, (r+1)*N/g) of the packed W)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED)
+    x = torch.randn(M, K, device=device, generator=g, dtype=torch.float32).to(torch.bfloat16)
+    w_norm = (torch.rand(K, device=device, generator=g) + 0.5).to(torch.bfloat16)
+    n_local = N // d.world
+    lo, hi = d.rank * n_local, (d.rank + 1) * n_local
+    gate = torch.empty(n_local, K, device=device, dtype=torch.bfloat16)
+    up = torch.empty(n_local, K, device=device, dtype=torch.bfloat16)
+    rows_per_chunk = 2048
+    for half, dst in ((0, gate), (1, up)):
+        for r0 in range(0, N, rows_per_chunk):  # generate W in chunks: same stream on every rank
+            chunk = torch.randn(rows_per_chunk, K, device=device, generator=g) * (K ** -0.5)
+            a, b = max(r0, lo), min(r0 + rows_per_chunk, hi)
+            if a < b:
+                dst[a - lo:b - lo] = chunk[a - r0:b - r0].to(torch.bfloat16)
+    packed = torch.cat((gate, up), dim=0).contiguous()
+    del gate, up
+    return {"x": x, "w_norm": w_norm, "packed": packed, "n_local": n_local}
+
+
+# ---------------------------------------------------------------- our arm
+
+
+def time_region(d: Dist, fn, steps: int, warmup: int) -> float:
+    """Max over ranks of the device time (ms) of `steps` calls of fn."""
+    for _ in range(warmup):
+        fn()
+    d.barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    end.synchronize()
+    ms = start.elapsed_time(end)
+    d.barrier()
+    return d.max(ms)
+
+
+def event_median_us(fn, reps: int, flush=None) -> float:
+    samples = []
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    for _ in range(reps):
+        if flush is not None:
+            flush()
+        start.record()
+        fn()
+        end.record()
+        end.synchronize()
+        samples.append(start.elapsed_time(end) * 1000.0)
+    return statistics.median(samples)
+
+
+def op_table(d: Dist, pk: dict) -> dict:
+    """Every other BASELINE config at N=1 (rank 0), plus the sharded large
+    RMSNorm and 2^30 reduction at every N.  Cold = L2 flushed before each rep."""
+    from cuda_operator_lab import bindings as b
+    from cuda_operator_lab.benchmarking import L2Flusher
+
+    dev = torch.device("cuda")
+    ops: dict = {}
+    hbm = pk["hbm_gbs"]
+    tc = pk["bf16_tflops"]
+    flush = L2Flusher(dev)
+
+    def mem_op(name, fn, nbytes, reps=50):
+        warm = event_median_us(fn, reps)
+        cold = event_median_us(fn, reps, flush)
+        ops[name] = {"us_warm": round(warm, 3), "us_cold": round(cold, 3),
+                     "gbs_cold": round(nbytes / cold / 1e3, 1),
+                     "frac_cold": round(nbytes / cold / 1e3 / hbm, 3), "bytes": nbytes}
+
+    def tc_op(name, fn, flops, reps=30):
+        us = event_median_us(fn, reps, flush)
+        ops[name] = {"us_cold": round(us, 3), "tflops": round(flops / us / 1e6, 1),
+                     "frac": round(flops / us / 1e6 / tc, 3), "flops": flops}
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 1)
+    # sharded at every N: RMSNorm bf16 rows [r*M/g, ...) and the 2^30 reduction chunk
+    rows = M // d.world
+    xs = torch.randn(rows, K, device=dev, generator=g).to(torch.bfloat16)
+    ws = (torch.rand(K, device=dev, generator=g) + 0.5).to(torch.bfloat16)
+    ys = torch.empty_like(xs)
+    nbytes = 2 * rows * K * 2 + K * 2
+    us = event_median_us(lambda: b.rmsnorm_bf16_into(xs, ws, ys, EPS), 50, flush)
+    us = d.max(us)
+    ops["rmsnorm_bf16_16384x4096_rowsharded"] = {
+        "us_per_rank": round(us, 3), "gbs_job": round(nbytes * d.world / us / 1e3, 1),
+        "frac_per_gpu": round(nbytes / us / 1e3 / hbm, 3)}
+    del xs, ys
+    chunk = REDUCTION_N // d.world
+    xr = torch.rand(chunk, device=dev, generator=g) * 2 - 1
+    partial = torch.empty(1, device=dev, dtype=torch.float64)
+
+    def reduce_step():
+        b.reduction_partial_f64_into(xr, partial)
+        if d.enabled:
+            d.dist.all_reduce(partial)
+        return partial.to(torch.float32)
+
+    us = d.max(event_median_us(reduce_step, 20))
+    ops["reduction_2^30_chunked_allreduce"] = {
+        "us": round(us, 3), "gbs_job": round(REDUCTION_N * 4 / us / 1e3, 1),
+        "frac_per_gpu": round(chunk * 4 / us / 1e3 / hbm, 3)}
+    del xr
+    if d.rank != 0 or d.world > 1:
+        return ops
+
+    # rank 0 at N=1: the single-GPU configs
+    def randn(*shape, scale=1.0):
+        return torch.randn(*shape, device=dev, generator=g) * scale
+
+    x = randn(128, 8192)
+    w = torch.rand(8192, device=dev, generator=g) + 0.5
+    y = torch.empty_like(x)
+    mem_op("rmsnorm_fp32_128x8192", lambda: b.rmsnorm_v4_into(x, w, y, EPS), 2 * x.numel() * 4 + 8192 * 4)
+    x = randn(128, 4096, scale=2.0)
+    y = torch.empty_like(x)
+    mem_op("softmax_fp32_128x4096", lambda: b.softmax_v5_into(x, y), 2 * x.numel() * 4)
+    gam = torch.rand(4096, device=dev, generator=g) + 0.5
+    bet = randn(4096, scale=0.1)
+    mem_op("layernorm_fp32_128x4096", lambda: b.layernorm_v5_into(x, gam, bet, y),
+           2 * x.numel() * 4 + 2 * 4096 * 4)
+    r = randn(128, 4096)
+    mem_op("residual_layernorm_fp32_128x4096", lambda: b.fused_residual_layernorm_v4_into(
+        x, r, gam, bet, y), 3 * x.numel() * 4 + 2 * 4096 * 4)
+    h = torch.empty_like(x)
+    mem_op("residual_layernorm_h_fp32_128x4096", lambda: b.fused_residual_layernorm_h_into(
+        x, r, gam, bet, h, y), 4 * x.numel() * 4 + 2 * 4096 * 4)
+    xr = torch.rand(16_777_216, device=dev, generator=g) * 2 - 1
+    s = torch.empty(1, device=dev)
+    mem_op("reduction_fp32_16777216", lambda: b.reduction_v5_into(xr, s), xr.numel() * 4)
+    x = randn(1024, 4096)
+    bias = randn(4096, scale=0.1)
+    y = torch.empty_like(x)
+    mem_op("bias_gelu_fp32_1024x4096", lambda: b.fused_bias_gelu_v2_into(x, bias, y),
+           2 * x.numel() * 4 + 4096 * 4)
+    u = randn(1024, 4096)
+    mem_op("swiglu_fp32_1024x4096", lambda: b.swiglu_v2_into(x, u, y), 3 * x.numel() * 4)
+
+    xb = randn(512, 4096).to(torch.bfloat16)
+    wb = randn(8192, 4096, scale=4096 ** -0.5).to(torch.bfloat16)
+    ws32 = torch.empty(512, 8192, device=dev)
+    o32 = torch.empty(512, 4096, device=dev)
+    ob = torch.empty(512, 4096, device=dev, dtype=torch.bfloat16)
+    fl = 2 * 512 * 4096 * 8192
+    tc_op("gemm_swiglu_bf16_512x4096x4096_fp32out_v11", lambda: b.gemm_swiglu_v11_into(xb, wb, ws32, o32), fl)
+    tc_op("gemm_swiglu_bf16_512x4096x4096_bf16out", lambda: b.gemm_swiglu_bf16_into(xb, wb, ob), fl)
+    xs_ = randn(128, 64).to(torch.bfloat16)
+    wsm = randn(4096, 64, scale=0.125).to(torch.bfloat16)
+    os_ = torch.empty(128, 2048, device=dev)
+    ws_ = torch.empty(128, 4096, device=dev)
+    us = event_median_us(lambda: b.gemm_swiglu_v11_into(xs_, wsm, ws_, os_), 100)
+    ops["gemm_swiglu_bf16_128x64x2048_v11"] = {"us_warm": round(us, 3),
+                                               "tflops": round(2 * 128 * 64 * 4096 / us / 1e6, 2)}
+    wg = randn(4096, 4096, scale=4096 ** -0.5).to(torch.bfloat16)
+    bg = randn(4096, scale=0.1)
+    og = torch.empty(512, 4096, device=dev, dtype=torch.bfloat16)
+    tc_op("gemm_bias_gelu_bf16_512x4096x4096", lambda: b.gemm_bias_gelu_bf16_into(xb, wg, bg, og),
+          2 * 512 * 4096 * 4096)
+    xf = randn(512, 4096)
+    wf = randn(4096, 4096, scale=4096 ** -0.5)
+    of = torch.empty(512, 4096, device=dev)
+    tc_op("gemm_bias_gelu_fp32_512x4096x4096_v6_cudacores", lambda: b.gemm_bias_gelu_v6_into(
+        xf, wf, bg, of), 2 * 512 * 4096 * 4096, reps=5)
+    return ops
+
+
+def run_ours(args, d: Dist) -> dict | None:
+    from cuda_operator_lab import bindings as b
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    pk = peaks()
+    inp = make_inputs(d, dev)
+    x, w_norm, packed, n_local = inp["x"], inp["w_norm"], inp["packed"], inp["n_local"]
+    xn = torch.empty_like(x)
+    out = torch.empty(M, n_local, device=dev, dtype=torch.bfloat16)
+
+    def step():
+        b.rmsnorm_bf16_into(x, w_norm, xn, EPS)
+        b.gemm_swiglu_bf16_into(xn, packed, out)
+
+    b.gemm_status(clear=True)
+    gpus = list(range(d.world))
+    with ClockSampler(gpus) as clocks:
+        ms = time_region(d, step, args.steps, args.warmup)
+    clock_info = clocks.summary() if d.rank == 0 else None
+    status = b.gemm_status(clear=True)
+    if status != 0:
+        raise RuntimeError(f"GEMM bounded wait timed out (status {status})")
+
+    # dominant kernel alone: average GEMM launch duration
+    gemm_steps = max(10, args.steps // 2)
+    gemm_ms = time_region(d, lambda: b.gemm_swiglu_bf16_into(xn, packed, out), gemm_steps, 3)
+    gemm_us = gemm_ms * 1000.0 / gemm_steps
+    flops_launch = 2 * M * K * 2 * n_local
+    achieved = flops_launch / gemm_us / 1e6
+    traffic = committed_traffic().get(f"gemm_swiglu_bf16_M{M}_K{K}_N{n_local}")
+
+    # e2e through the public API: pinned host X in, output shard back, every step
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        b.rmsnorm_bf16_into(x_dev, w_norm, xn, EPS)
+        b.gemm_swiglu_bf16_into(xn, packed, out)
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_steps = max(5, args.steps // 20)
+    e2e_ms = time_region(d, e2e_step, e2e_steps, 2)
+    torch.testing.assert_close(out_host[:4].float(), out[:4].cpu().float())
+    del x_host, out_host, x_dev
+
+    ops = op_table(d, pk) if not args.skip_ops else {}
+
+    cpu = None
+    if d.rank == 0 and d.world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if d.rank != 0:
+        return None
+    value = GEMM_FLOPS * args.steps / (ms / 1e3) / 1e12
+    return {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": d.world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) X, N(0,1/K) W, U(0.5,1.5) norm weight)",
+        "config": {"workload": "llama_mlp_block (BASELINE config 5)", "M": M, "K": K, "N": N,
+                   "rmsnorm": "bf16 [16384,4096], replicated on every rank",
+                   "gemm": "packed GEMM+SwiGLU bf16 out, N-sharded",
+                   "parallelism": f"N-shard x{d.world}" if d.world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (X 134 MB, W 235 MB); no flush"},
+        "e2e": {"value": round(GEMM_FLOPS * e2e_steps / (e2e_ms / 1e3) / 1e12, 2),
+                "unit": "TFLOP/s", "h2d_bytes_per_step": M * K * 2 * d.world,
+                "d2h_bytes_per_step": M * N * 2},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
+                     "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": round(achieved / pk["bf16_tflops_sustained"], 3),
+                     "traffic": traffic, "kernel": "gemm_bf16_tc_kernel (SwiGLU, bf16 out)",
+                     "peak_source": f"{pk['source']} sustained bf16",
+                     "gemm_us_per_launch": round(gemm_us, 2)},
+        "cpu_baseline": cpu,
+        "clocks": clock_info,
+        "gpu_launches": 2 * args.steps,
+        "ops": ops,
+    }
+
+
+# ---------------------------------------------------------------- CPU baseline
+
+
+class CpuPath:
+    """The reference's CPU path (the oracle restating references.py) on a row
+    sample of the workload: RMSNorm + packed GEMM+SwiGLU of `rows` rows of X
+    against the full W, with every host thread."""
+
+    def __init__(self) -> None:
+        from oracle import reference_math as oracle
+
+        self.oracle = oracle
+        torch.set_num_threads(os.cpu_count() or 1)
+        g = torch.Generator()
+        g.manual_seed(SEED)
+        self.x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+        self.w_norm = (torch.rand(K, generator=g) + 0.5).to(torch.bfloat16)
+        self.packed = (torch.randn(2 * N, K, generator=g) * K ** -0.5).to(torch.bfloat16)
+
+    def run(self, rows: int) -> float:
+        t0 = time.perf_counter()
+        self.oracle.mlp_block_bf16(self.x[:rows], self.w_norm, self.packed, EPS)
+        return time.perf_counter() - t0
+
+    def rows_for(self, seconds: float) -> int:
+        """Rows whose pass takes about `seconds` (calibrated on 64 rows)."""
+        self.run(16)
+        t = self.run(64)
+        return int(max(16, min(M, 64 * seconds / max(t, 1e-6))))
+
+    def sample(self, rows: int) -> dict:
+        dt = self.run(rows)
+        flops = 2 * rows * K * 2 * N
+        return {"value": round(flops / dt / 1e12, 4), "unit": "TFLOP/s",
+                "cores": torch.get_num_threads(), "kind": "port",
+                "sample": f"{rows} of {M} rows of X against the full W, one pass ({dt:.2f} s)"}
+
+
+def cpu_baseline(seconds: float = 15.0) -> dict:
+    path = CpuPath()
+    return path.sample(path.rows_for(seconds))
+
+
+def run_reference(args) -> dict:
+    path = CpuPath()
+    budget = 150.0 / (args.steps + args.warmup)  # whole run within a few minutes
+    rows = path.rows_for(min(10.0, budget))
+    for _ in range(args.warmup):
+        path.run(max(16, rows // 4))
+    samples = [path.sample(rows) for _ in range(args.steps)]
+    value = statistics.median(s["value"] for s in samples)
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", str(args.gpus))),
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(2 * rows * K * 2 * N / (value * 1e12) * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "llama_mlp_block (BASELINE config 5)", "M": M, "K": K, "N": N,
+                   "sample_rows_per_step": rows,
+                   "path": "reference CPU math (oracle port of references.py) on host cores"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": samples[0]["cores"],
+                         "kind": "port", "sample": samples[0]["sample"]},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__,
+                                     formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=300)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--cpu-seconds", type=float, default=15.0)
+    parser.add_argument("--skip-ops", action="store_true")
+    parser.add_argument("--skip-cpu", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be >= 3")
+
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) != 0:
+            return  # rank 0 alone times the CPU path
+        print(json.dumps(run_reference(args)))
+        return
+
+    d = Dist()
+    if d.world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={d.world}")
+    try:
+        result = run_ours(args, d)
+    finally:
+        d.close()
+    if result is not None:
+        print(json.dumps(result))
+
+
+if __name__ == "__main__":
+    main()

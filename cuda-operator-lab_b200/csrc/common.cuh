@@ -1,0 +1,130 @@
+// Shared host/device helpers for the sm_100a operator library.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <mutex>
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/cuda_operator_lab.h"
+
+#define COL_API extern "C" __attribute__((visibility("default")))
+
+namespace col {
+
+// Library-specific return codes (cudaError_t values stay below 10000).
+constexpr int kErrNoTensorMapEncoder = 10001;   // driver lacks cuTensorMapEncodeTiled
+constexpr int kErrTensorMapEncode = 10002;      // cuTensorMapEncodeTiled rejected a map
+constexpr int kErrDeviceNotSupported = 10003;   // device is not sm_100
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) {
+  return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0u;
+}
+
+// Per-device properties read once (thread safe); the library never queries
+// device attributes on the launch path after the first call on a device.
+struct DeviceInfo {
+  int sm_count = 0;
+  int cc_major = 0;
+  int cc_minor = 0;
+  int max_smem_optin = 0;
+};
+
+inline const DeviceInfo& device_info(int* device_out = nullptr) {
+  constexpr int kMaxDevices = 64;
+  static DeviceInfo infos[kMaxDevices];
+  static std::once_flag flags[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) dev = 0;
+  std::call_once(flags[dev], [dev]() {
+    DeviceInfo info;
+    cudaDeviceGetAttribute(&info.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&info.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&info.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&info.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (info.sm_count <= 0) info.sm_count = 148;
+    infos[dev] = info;
+  });
+  if (device_out) *device_out = dev;
+  return infos[dev];
+}
+
+// ---------------------------------------------------------------- device math
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_f64(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// silu(x) = x / (1 + exp(-x)), the form of swiglu.cu:11-13.
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
+
+// Exact GELU, 0.5 x (1 + erf(x / sqrt 2)) (fused_bias_gelu.cu:12-14).
+__device__ __forceinline__ float gelu_erf_f(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+}
+
+// tanh-approximate GELU, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),
+// the form torch.nn.functional.gelu(approximate="tanh") and the reference's
+// GELU_BIAS GEMM versions (v2..v6) produce.
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// Streaming 16-byte loads/stores (read-once inputs, write-once outputs).
+__device__ __forceinline__ float4 ld_stream_f4(const float4* p) { return __ldcs(p); }
+__device__ __forceinline__ uint4 ld_stream_u4(const uint4* p) { return __ldcs(p); }
+__device__ __forceinline__ void st_stream_f4(float4* p, float4 v) { __stcs(p, v); }
+__device__ __forceinline__ void st_stream_u4(uint4* p, uint4 v) { __stcs(p, v); }
+
+__device__ __forceinline__ void unpack_bf16x8(uint4 v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&f)[8]) {
+  uint4 v;
+  v.x = pack_bf16x2(f[0], f[1]);
+  v.y = pack_bf16x2(f[2], f[3]);
+  v.z = pack_bf16x2(f[4], f[5]);
+  v.w = pack_bf16x2(f[6], f[7]);
+  return v;
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+}  // namespace col

@@ -1,0 +1,503 @@
+// Blackwell (sm_100a) tensor-core GEMM with fused SwiGLU / bias+GELU
+// epilogues: D[M, N'] = X[M, K] . B[N', K]^T, bf16 operands, fp32 accumulate.
+//
+// Persistent, warp-specialised CTA (256 threads, one CTA per SM):
+//   warp 0      TMA producer: one thread streams 128x64 X tiles and two
+//               BNHx64 B boxes per k-block into a STAGES-deep smem ring
+//               (128-byte swizzle, completion counted on an mbarrier);
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=2*BNH,
+//               K=16) from the smem descriptors into a TMEM accumulator and
+//               releases ring slots with tcgen05.commit;
+//   warp 2      allocates/frees the TMEM columns;
+//   warps 4..7  epilogue: tcgen05.ld the accumulator (one row per thread),
+//               apply silu(g)*u or gelu(acc+bias) in registers, store once.
+// Two TMEM accumulators alternate between tiles, so the epilogue of tile i
+// overlaps the main loop of tile i+1.
+//
+// SwiGLU pairing: the B stage holds the gate box (rows n0..n0+BNH of Wg) and
+// the up box (the same rows of Wu) back to back, so one MMA of N = 2*BNH puts
+// gate columns in accumulator columns [0, BNH) and up columns in [BNH, 2*BNH).
+// For bias+GELU both boxes come from W (rows n0.. and n0+BNH..), giving 2*BNH
+// output columns per tile.
+//
+// Every mbarrier wait is bounded (kWaitLimitNs); on timeout the waiting
+// thread ORs a code into the device status word, raises a CTA-wide abort
+// flag that the other roles poll, and all roles drain in-flight copies and
+// MMAs (again with bounded waits) before TMEM is freed and the CTA exits.
+#pragma once
+
+#include <cuda.h>
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace col {
+namespace sm100 {
+
+enum Epilogue : int {
+  kEpiSwiGLU = 0,           // out = silu(g) * u
+  kEpiSwiGLURoundBf16 = 1,  // g, u rounded to bf16 first (bf16 GEMM workspace semantics)
+  kEpiBiasGeluErf = 2,      // out = gelu_erf(acc + bias[n])
+  kEpiBiasGeluTanh = 3,     // out = gelu_tanh(acc + bias[n])
+};
+
+constexpr int kBlockM = 128;
+constexpr int kBlockK = 64;  // bf16 elements per k-block: one 128-byte swizzle row
+constexpr int kGroupM = 16;  // m-blocks per rasterisation group (L2 reuse of B)
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+// Status bits written on a bounded-wait timeout.
+constexpr unsigned kStatusProducer = 1u;
+constexpr unsigned kStatusMma = 2u;
+constexpr unsigned kStatusEpilogue = 4u;
+constexpr unsigned kStatusDrain = 8u;
+
+struct __align__(64) GemmParams {
+  CUtensorMap map_a;   // X [M, K]
+  CUtensorMap map_b0;  // gate rows (SwiGLU) or W rows (GELU)
+  CUtensorMap map_b1;  // up rows (SwiGLU) or W rows (GELU)
+  const float* bias;
+  void* out;
+  unsigned* status;
+  int m;
+  int n;  // output columns
+  int k;
+  int num_m_blocks;
+  int num_n_blocks;
+  int num_k_blocks;
+  int b_row_stride;   // B rows advanced per n-block (box 0)
+  int b1_row_offset;  // box-1 row relative to box 0
+  int out_ld;         // output row stride in elements
+  int out_vec_ok;     // 16-byte vector stores allowed
+};
+
+template <int BNH>
+struct TileCfg {
+  static constexpr int kMmaN = 2 * BNH;
+  static constexpr uint32_t kABytes = kBlockM * kBlockK * 2;
+  static constexpr uint32_t kBBytes = kMmaN * kBlockK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = BNH == 128 ? 4 : 6;
+  static constexpr uint32_t kAccCols = kMmaN;
+  static constexpr uint32_t kTmemCols = 2 * kAccCols;
+  static constexpr uint32_t kBarrierBytes = 256;
+  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+};
+
+// ------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait: true when the phase of `parity` completed; false after the
+// time limit or when another role raised the abort flag.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+  }
+}
+
+// Bounded wait that ignores the abort flag (used while draining).
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t holder, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(holder),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
+               : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with the
+// 128-byte swizzle: 8-row core groups 1024 bytes apart (SBO), leading offset
+// unused for swizzled K-major tiles (encoded as 16 bytes), version 1, layout
+// SWIZZLE_128B (2).  Tile bases are 1024-byte aligned.
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor, kind::f16: D fp32, A and B bf16, both K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+// 32 consecutive fp32 accumulator columns of this thread's TMEM lane; the
+// wait is in the same asm block so no use of r[] can be scheduled before the
+// asynchronous load has landed.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// ------------------------------------------------------------ tile schedule
+
+__device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& mb, int& nb) {
+  const int group_tiles = kGroupM * p.num_n_blocks;
+  const int group = tile / group_tiles;
+  const int first_m = group * kGroupM;
+  const int rows = min(p.num_m_blocks - first_m, kGroupM);
+  const int in_group = tile - group * group_tiles;
+  mb = first_m + in_group % rows;
+  nb = in_group / rows;
+}
+
+// ------------------------------------------------------------ epilogue store
+
+template <typename TOut>
+__device__ __forceinline__ void store_chunk32(const GemmParams& p, int row, int col0,
+                                              const float (&o)[32]) {
+  if (row >= p.m) return;
+  TOut* dst = static_cast<TOut*>(p.out) + static_cast<std::size_t>(row) * p.out_ld + col0;
+  if (p.out_vec_ok && col0 + 32 <= p.n) {
+    if constexpr (sizeof(TOut) == 4) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        __stcs(d4 + j, make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]));
+      }
+    } else {
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 v;
+        v.x = pack_bf16x2(o[8 * j + 0], o[8 * j + 1]);
+        v.y = pack_bf16x2(o[8 * j + 2], o[8 * j + 3]);
+        v.z = pack_bf16x2(o[8 * j + 4], o[8 * j + 5]);
+        v.w = pack_bf16x2(o[8 * j + 6], o[8 * j + 7]);
+        __stcs(d4 + j, v);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (col0 + j < p.n) {
+        if constexpr (sizeof(TOut) == 4) {
+          dst[j] = o[j];
+        } else {
+          dst[j] = __float2bfloat16_rn(o[j]);
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------ the kernel
+
+template <int BNH, int EPI, typename TOut>
+__global__ void __launch_bounds__(256, 1) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
+  using Cfg = TileCfg<BNH>;
+  constexpr int kStages = Cfg::kStages;
+  constexpr uint32_t kIdesc = idesc_bf16_f32(kBlockM, Cfg::kMmaN);
+  constexpr bool kSwiGLU = (EPI == kEpiSwiGLU || EPI == kEpiSwiGLURoundBf16);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) & ~static_cast<std::uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * Cfg::kStageBytes);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + kStages;
+  uint64_t* tfull_bar = bars + 2 * kStages;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(full_bar + s), 1);
+      mbar_init(smem_u32(empty_bar + s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(tfull_bar + a), 1);
+      mbar_init(smem_u32(tempty_bar + a), 4);
+    }
+    mbar_init(smem_u32(drain_bar), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 2) tmem_alloc(smem_u32(tmem_holder), Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  auto fail = [&](unsigned code) {
+    atomicOr(p.status, code);
+    *abort_flag = 1;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      prefetch_tmap(&p.map_a);
+      prefetch_tmap(&p.map_b0);
+      prefetch_tmap(&p.map_b1);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0;  // stages holding a copy that may be in flight
+      uint32_t issued_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        const int a_row = mb * kBlockM;
+        const int b0_row = nb * p.b_row_stride;
+        const int b1_row = b0_row + p.b1_row_offset;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1u, abort_flag)) {
+            fail(kStatusProducer);
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+          const uint32_t sb = sa + Cfg::kABytes;
+          const uint32_t fb = smem_u32(full_bar + stage);
+          mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
+          const int kx = kb * kBlockK;
+          tma_load_2d(sa, &p.map_a, fb, kx, a_row);
+          tma_load_2d(sb, &p.map_b0, fb, kx, b0_row);
+          tma_load_2d(sb + BNH * 128, &p.map_b1, fb, kx, b1_row);
+          issued_mask |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok || *abort_flag) {
+        // Drain: every copy this thread issued must land before the CTA exits.
+        for (int s = 0; s < kStages; ++s) {
+          if (issued_mask & (1u << s)) {
+            if (!mbar_wait_drain(smem_u32(full_bar + s), (issued_phase >> s) & 1u)) {
+              atomicOr(p.status, kStatusDrain);
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1u, abort_flag)) {
+          fail(kStatusMma);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
+            fail(kStatusMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+          const uint32_t sb = sa + Cfg::kABytes;
+#pragma unroll
+          for (int k = 0; k < kBlockK / 16; ++k) {
+            umma_bf16(d_tmem, sdesc_kmajor_sw128(sa + k * 32), sdesc_kmajor_sw128(sb + k * 32),
+                      kIdesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(smem_u32(empty_bar + stage));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(tfull_bar + acc));
+      }
+      // All MMAs this thread issued must finish before TMEM is released.
+      if (issued_any) {
+        umma_commit(smem_u32(drain_bar));
+        if (!mbar_wait_drain(smem_u32(drain_bar), 0)) atomicOr(p.status, kStatusDrain);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- epilogue: warp (4 + q) owns TMEM lanes [32q, 32q + 32)
+    const int q = warp - 4;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      // All lanes wait, then agree, so the warp-collective tcgen05.ld below
+      // always runs with the full warp.
+      const bool got = mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) {
+        if (lane == 0) fail(kStatusEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const int row = mb * kBlockM + q * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
+      if constexpr (kSwiGLU) {
+        const int col_base = nb * BNH;
+#pragma unroll 1
+        for (int c = 0; c < BNH; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(t_row + c, g);
+          tmem_ld32(t_row + BNH + c, u);
+          float o[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float gv = __uint_as_float(g[j]);
+            float uv = __uint_as_float(u[j]);
+            if constexpr (EPI == kEpiSwiGLURoundBf16) {
+              gv = bf16_round(gv);
+              uv = bf16_round(uv);
+            }
+            o[j] = silu_f(gv) * uv;
+          }
+          store_chunk32<TOut>(p, row, col_base + c, o);
+        }
+      } else {
+        const int col_base = nb * 2 * BNH;
+#pragma unroll 1
+        for (int c = 0; c < 2 * BNH; c += 32) {
+          uint32_t a[32];
+          tmem_ld32(t_row + c, a);
+          float o[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int colj = col_base + c + j;
+            const float bv = colj < p.n ? __ldg(p.bias + colj) : 0.0f;
+            const float z = __uint_as_float(a[j]) + bv;
+            if constexpr (EPI == kEpiBiasGeluErf) {
+              o[j] = gelu_erf_f(z);
+            } else {
+              o[j] = gelu_tanh_f(z);
+            }
+          }
+          store_chunk32<TOut>(p, row, col_base + c, o);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(tempty_bar + acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace sm100
+}  // namespace col

@@ -1,0 +1,182 @@
+// Pointwise fused ops: bias + exact GELU (fused_bias_gelu.cuh:5-29) and
+// SwiGLU (swiglu.cuh:5-27).  Both are pure HBM streams: 16-byte loads and
+// stores, several independent vectors in flight per thread, and a grid of a
+// few CTAs per SM that strides over the tensor.
+#include "common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;  // independent 16-byte vectors in flight per thread
+
+unsigned grid_for(std::uint64_t work_items, int per_thread) {
+  const std::uint64_t per_cta = static_cast<std::uint64_t>(kThreads) * per_thread;
+  std::uint64_t blocks = (work_items + per_cta - 1) / per_cta;
+  const std::uint64_t cap = static_cast<std::uint64_t>(col::device_info().sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks == 0) blocks = 1;
+  return static_cast<unsigned>(blocks);
+}
+
+// ---------------------------------------------------------------- SwiGLU
+
+__global__ void __launch_bounds__(kThreads)
+swiglu_vec_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
+                  float4* __restrict__ o, std::uint64_t nvec) {
+  const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
+  std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
+    float4 gv[kUnroll], uv[kUnroll];
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) {
+      gv[j] = col::ld_stream_f4(g + i + j * stride);
+      uv[j] = col::ld_stream_f4(u + i + j * stride);
+    }
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) {
+      float4 r;
+      r.x = col::silu_f(gv[j].x) * uv[j].x;
+      r.y = col::silu_f(gv[j].y) * uv[j].y;
+      r.z = col::silu_f(gv[j].z) * uv[j].z;
+      r.w = col::silu_f(gv[j].w) * uv[j].w;
+      col::st_stream_f4(o + i + j * stride, r);
+    }
+  }
+  for (; i < nvec; i += stride) {
+    const float4 gv = col::ld_stream_f4(g + i);
+    const float4 uv = col::ld_stream_f4(u + i);
+    col::st_stream_f4(o + i, make_float4(col::silu_f(gv.x) * uv.x, col::silu_f(gv.y) * uv.y,
+                                         col::silu_f(gv.z) * uv.z, col::silu_f(gv.w) * uv.w));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+swiglu_scalar_kernel(const float* __restrict__ g, const float* __restrict__ u,
+                     float* __restrict__ o, std::uint64_t begin, std::uint64_t n) {
+  const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
+  for (std::uint64_t i = begin + static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+       i < n; i += stride) {
+    o[i] = col::silu_f(g[i]) * u[i];
+  }
+}
+
+int swiglu_launch(const float* g, const float* u, float* o, std::uint64_t n, cudaStream_t s) {
+  std::uint64_t done = 0;
+  if (col::aligned16(g) && col::aligned16(u) && col::aligned16(o)) {
+    const std::uint64_t nvec = n / 4;
+    if (nvec) {
+      swiglu_vec_kernel<<<grid_for(nvec, kUnroll), kThreads, 0, s>>>(
+          reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(u),
+          reinterpret_cast<float4*>(o), nvec);
+      done = nvec * 4;
+    }
+  }
+  if (done < n) {
+    swiglu_scalar_kernel<<<grid_for(n - done, 1), kThreads, 0, s>>>(g, u, o, done, n);
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------- bias + GELU
+
+// Each CTA walks whole rows, so the bias column of a vector is its position
+// in the row (no per-element modulo); the bias row stays in L1.
+__global__ void __launch_bounds__(kThreads)
+bias_gelu_vec_kernel(const float4* __restrict__ x, const float4* __restrict__ b,
+                     float4* __restrict__ o, std::uint64_t rows, std::uint32_t vcols) {
+  const std::uint64_t total = rows * vcols;
+  const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
+  std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  for (; i + (kUnroll - 1) * stride < total; i += kUnroll * stride) {
+    float4 xv[kUnroll];
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) xv[j] = col::ld_stream_f4(x + i + j * stride);
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) {
+      const std::uint64_t idx = i + j * stride;
+      const float4 bv = __ldg(b + static_cast<std::uint32_t>(idx % vcols));
+      float4 r;
+      r.x = col::gelu_erf_f(xv[j].x + bv.x);
+      r.y = col::gelu_erf_f(xv[j].y + bv.y);
+      r.z = col::gelu_erf_f(xv[j].z + bv.z);
+      r.w = col::gelu_erf_f(xv[j].w + bv.w);
+      col::st_stream_f4(o + idx, r);
+    }
+  }
+  for (; i < total; i += stride) {
+    const float4 xv = col::ld_stream_f4(x + i);
+    const float4 bv = __ldg(b + static_cast<std::uint32_t>(i % vcols));
+    col::st_stream_f4(o + i, make_float4(col::gelu_erf_f(xv.x + bv.x), col::gelu_erf_f(xv.y + bv.y),
+                                         col::gelu_erf_f(xv.z + bv.z), col::gelu_erf_f(xv.w + bv.w)));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+bias_gelu_scalar_kernel(const float* __restrict__ x, const float* __restrict__ b,
+                        float* __restrict__ o, std::uint64_t rows, std::uint32_t cols) {
+  const std::uint64_t total = rows * cols;
+  const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
+  for (std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+       i < total; i += stride) {
+    o[i] = col::gelu_erf_f(x[i] + __ldg(b + static_cast<std::uint32_t>(i % cols)));
+  }
+}
+
+int bias_gelu(const float* x, const float* b, float* o, std::uint64_t rows, std::uint64_t cols,
+              void* stream) {
+  // fused_bias_gelu.cu:54-66: rows == 0 succeeds first; NULL or cols == 0 fail.
+  if (rows == 0) return 0;
+  if (x == nullptr || b == nullptr || o == nullptr || cols == 0 || cols > 0xffffffffull) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  const cudaStream_t s = col::as_stream(stream);
+  const std::uint32_t c = static_cast<std::uint32_t>(cols);
+  if ((c % 4) == 0 && col::aligned16(x) && col::aligned16(b) && col::aligned16(o)) {
+    const std::uint32_t vcols = c / 4;
+    bias_gelu_vec_kernel<<<grid_for(rows * vcols, kUnroll), kThreads, 0, s>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(b),
+        reinterpret_cast<float4*>(o), rows, vcols);
+  } else {
+    bias_gelu_scalar_kernel<<<grid_for(rows * c, 1), kThreads, 0, s>>>(x, b, o, rows, c);
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+COL_API int cuda_operator_fused_bias_gelu_v0(const float* input, const float* bias, float* output,
+                                             uint64_t rows, uint64_t cols, void* stream) {
+  return bias_gelu(input, bias, output, rows, cols, stream);
+}
+COL_API int cuda_operator_fused_bias_gelu_v1(const float* input, const float* bias, float* output,
+                                             uint64_t rows, uint64_t cols, void* stream) {
+  return bias_gelu(input, bias, output, rows, cols, stream);
+}
+COL_API int cuda_operator_fused_bias_gelu_v2(const float* input, const float* bias, float* output,
+                                             uint64_t rows, uint64_t cols, void* stream) {
+  return bias_gelu(input, bias, output, rows, cols, stream);
+}
+
+// swiglu.cu:50-61 (v0/v1): elements == 0 succeeds first; NULL fails.
+COL_API int cuda_operator_swiglu_v0(const float* gate, const float* up, float* output,
+                                    uint64_t elements, void* stream) {
+  if (elements == 0) return 0;
+  if (gate == nullptr || up == nullptr || output == nullptr) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  return swiglu_launch(gate, up, output, elements, col::as_stream(stream));
+}
+COL_API int cuda_operator_swiglu_v1(const float* gate, const float* up, float* output,
+                                    uint64_t elements, void* stream) {
+  return cuda_operator_swiglu_v0(gate, up, output, elements, stream);
+}
+// swiglu.cu:115-128 (v2): rows*cols == 0 succeeds first; NULL or cols == 0 fail.
+COL_API int cuda_operator_swiglu_v2(const float* gate, const float* up, float* output,
+                                    uint64_t rows, uint64_t cols, void* stream) {
+  const std::uint64_t elements = rows * cols;
+  if (elements == 0) return 0;
+  if (gate == nullptr || up == nullptr || output == nullptr || cols == 0) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  return swiglu_launch(gate, up, output, elements, col::as_stream(stream));
+}

@@ -1,0 +1,53 @@
+// RMSNorm entry points: the reference's fp32 v0..v4 (rmsnorm.cuh:5-47) and
+// the bf16 variant of the Llama MLP workload.
+#include "rowwise.cuh"
+
+namespace {
+
+int rmsnorm_f32(const float* x, const float* w, float* y, std::uint64_t rows,
+                std::uint64_t cols, float eps, void* stream) {
+  if (rows == 0) return 0;
+  if (x == nullptr || w == nullptr || y == nullptr || !col::row_dims_ok(rows, cols)) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  if (!(eps > 0.0f)) return static_cast<int>(cudaErrorInvalidValue);
+  col::RowArgs a{x, nullptr, w, nullptr, y, nullptr, rows, static_cast<std::uint32_t>(cols), eps};
+  return col::launch_rows<col::RowOp::kRms, float, false>(a, col::as_stream(stream));
+}
+
+}  // namespace
+
+COL_API int cuda_operator_rmsnorm_v0(const float* input, const float* weight, float* output,
+                                     uint64_t rows, uint64_t cols, float eps, void* stream) {
+  return rmsnorm_f32(input, weight, output, rows, cols, eps, stream);
+}
+COL_API int cuda_operator_rmsnorm_v1(const float* input, const float* weight, float* output,
+                                     uint64_t rows, uint64_t cols, float eps, void* stream) {
+  return rmsnorm_f32(input, weight, output, rows, cols, eps, stream);
+}
+COL_API int cuda_operator_rmsnorm_v2(const float* input, const float* weight, float* output,
+                                     uint64_t rows, uint64_t cols, float eps, void* stream) {
+  return rmsnorm_f32(input, weight, output, rows, cols, eps, stream);
+}
+COL_API int cuda_operator_rmsnorm_v3(const float* input, const float* weight, float* output,
+                                     uint64_t rows, uint64_t cols, float eps, void* stream) {
+  return rmsnorm_f32(input, weight, output, rows, cols, eps, stream);
+}
+COL_API int cuda_operator_rmsnorm_v4(const float* input, const float* weight, float* output,
+                                     uint64_t rows, uint64_t cols, float eps, void* stream) {
+  return rmsnorm_f32(input, weight, output, rows, cols, eps, stream);
+}
+
+COL_API int cuda_operator_rmsnorm_bf16(const void* input_bf16, const void* weight_bf16,
+                                       void* output_bf16, uint64_t rows, uint64_t cols, float eps,
+                                       void* stream) {
+  if (rows == 0) return 0;
+  if (input_bf16 == nullptr || weight_bf16 == nullptr || output_bf16 == nullptr ||
+      !col::row_dims_ok(rows, cols)) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  if (!(eps > 0.0f)) return static_cast<int>(cudaErrorInvalidValue);
+  col::RowArgs a{input_bf16, nullptr, weight_bf16, nullptr, output_bf16, nullptr, rows,
+                 static_cast<std::uint32_t>(cols), eps};
+  return col::launch_rows<col::RowOp::kRms, __nv_bfloat16, false>(a, col::as_stream(stream));
+}

@@ -1,0 +1,911 @@
+"""ctypes bindings for the sm_100a operator library (drop-in for the reference).
+
+Same public functions, arguments, validation messages, stream semantics and
+return conventions as the reference module ``python/cuda_operator_lab/
+bindings.py`` (its line numbers are cited per family below): every
+``<op>_v<k>_into`` validates PyTorch CUDA tensors on the host, passes their
+raw device pointers and ``torch.cuda.current_stream(x.device)`` to one
+``extern "C"`` symbol of ``libcuda_operator_lab.so`` (declared in
+``include/cuda_operator_lab.h``) and raises ``RuntimeError("CUDA error
+{code}: {message}")`` on a non-zero return; ``<op>_v<k>`` allocates the
+output and calls ``_into``.
+
+There is no fallback: if the shared library is missing, the first call raises
+``RuntimeError``.  ``CUDA_OPERATOR_LIB`` overrides the library path
+(reference ``bindings.py:17-21``).
+
+Functions after the reference set (``rmsnorm_bf16``,
+``fused_residual_layernorm_h``, ``gemm_swiglu_bf16``, ``gemm_bias_gelu_bf16``,
+``reduction_partial_f64``) expose the library's additional entry points.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Callable
+
+import torch
+
+__all__: list[str] = []
+
+# ---------------------------------------------------------------- library
+
+_P = ctypes.c_void_p
+_U64 = ctypes.c_uint64
+_F32 = ctypes.c_float
+_I32 = ctypes.c_int
+
+# symbol -> argtypes (restype int unless listed in _RESTYPES)
+_SIGNATURES: dict[str, list] = {}
+for _v in range(6):
+    _SIGNATURES[f"cuda_operator_reduction_v{_v}"] = [_P, _P, _U64, _P]
+    _SIGNATURES[f"cuda_operator_softmax_v{_v}"] = [_P, _P, _U64, _U64, _P]
+    _SIGNATURES[f"cuda_operator_layernorm_v{_v}"] = [_P, _P, _P, _P, _U64, _U64, _F32, _P]
+for _v in range(5):
+    _SIGNATURES[f"cuda_operator_rmsnorm_v{_v}"] = [_P, _P, _P, _U64, _U64, _F32, _P]
+    _SIGNATURES[f"cuda_operator_fused_residual_layernorm_v{_v}"] = [
+        _P, _P, _P, _P, _P, _U64, _U64, _F32, _P]
+for _v in range(3):
+    _SIGNATURES[f"cuda_operator_fused_bias_gelu_v{_v}"] = [_P, _P, _P, _U64, _U64, _P]
+_SIGNATURES["cuda_operator_swiglu_v0"] = [_P, _P, _P, _U64, _P]
+_SIGNATURES["cuda_operator_swiglu_v1"] = [_P, _P, _P, _U64, _P]
+_SIGNATURES["cuda_operator_swiglu_v2"] = [_P, _P, _P, _U64, _U64, _P]
+for _v in range(7):
+    _SIGNATURES[f"cuda_operator_gemm_bias_gelu_v{_v}"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
+for _v in (0, 1):
+    _SIGNATURES[f"cuda_operator_gemm_swiglu_v{_v}"] = [_P, _P, _P, _P, _P, _U64, _U64, _U64, _P]
+for _v in (2, 3, 4, 5, 10, 11):
+    _SIGNATURES[f"cuda_operator_gemm_swiglu_v{_v}"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
+for _v in (6, 7, 8, 9):
+    _SIGNATURES[f"cuda_operator_gemm_swiglu_v{_v}"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
+_SIGNATURES["cuda_operator_error_string"] = [_I32]
+# entry points new in this library
+_SIGNATURES["cuda_operator_rmsnorm_bf16"] = [_P, _P, _P, _U64, _U64, _F32, _P]
+_SIGNATURES["cuda_operator_fused_residual_layernorm_h"] = [
+    _P, _P, _P, _P, _P, _P, _U64, _U64, _F32, _P]
+_SIGNATURES["cuda_operator_gemm_swiglu_bf16"] = [_P, _P, _P, _U64, _U64, _U64, _P]
+_SIGNATURES["cuda_operator_gemm_bias_gelu_bf16"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
+_SIGNATURES["cuda_operator_reduction_partial_f64"] = [_P, _P, _U64, _P]
+_SIGNATURES["cuda_operator_lab_device_info"] = [_P, _P, _P]
+_SIGNATURES["cuda_operator_lab_build_tag"] = []
+_SIGNATURES["cuda_operator_lab_gemm_status"] = [_P, _I32]
+
+_RESTYPES = {
+    "cuda_operator_error_string": ctypes.c_char_p,
+    "cuda_operator_lab_build_tag": ctypes.c_char_p,
+}
+
+#: The 54 symbols of the reference library (``bindings.py:32-417``).
+REFERENCE_SYMBOLS = tuple(
+    name for name in _SIGNATURES
+    if name.startswith("cuda_operator_") and not name.startswith("cuda_operator_lab_")
+    and not name.endswith(("_bf16", "_h", "_partial_f64"))
+)
+
+
+def _default_library_path() -> Path:
+    override = os.environ.get("CUDA_OPERATOR_LIB")
+    if override:
+        return Path(override).expanduser().resolve()
+    return Path(__file__).resolve().parents[1] / "build" / "lib" / "libcuda_operator_lab.so"
+
+
+class _Library:
+    """The loaded shared library with argtypes declared for every symbol.
+
+    Like the reference (``bindings.py:24-31``) every symbol is resolved
+    eagerly, so a library that lacks one fails at load time, not mid-run.
+    """
+
+    def __init__(self, path: Path) -> None:
+        if not path.is_file():
+            raise RuntimeError(
+                f"CUDA operator library not found at {path}. "
+                "Build it with `python cuda-operator-lab_b200/build.py`."
+            )
+        self.path = path
+        self.handle = ctypes.CDLL(str(path))
+        for name, argtypes in _SIGNATURES.items():
+            function = getattr(self.handle, name)
+            function.argtypes = argtypes
+            function.restype = _RESTYPES.get(name, ctypes.c_int)
+
+    def check(self, code: int) -> None:
+        if code == 0:
+            return
+        message = self.handle.cuda_operator_error_string(code)
+        decoded = message.decode("utf-8", errors="replace") if message else "unknown CUDA error"
+        raise RuntimeError(f"CUDA error {code}: {decoded}")
+
+
+_LIBRARY: _Library | None = None
+
+
+def _library() -> _Library:
+    global _LIBRARY
+    if _LIBRARY is None:
+        _LIBRARY = _Library(_default_library_path())
+    return _LIBRARY
+
+
+def library_path() -> Path:
+    """Path of the shared library the bindings load."""
+    return _default_library_path()
+
+
+def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device=t.device).cuda_stream)
+
+
+def _call(symbol: str, *args) -> None:
+    library = _library()
+    library.check(getattr(library.handle, symbol)(*args))
+
+
+def _export(name: str, fn: Callable, doc: str) -> Callable:
+    fn.__name__ = name
+    fn.__qualname__ = name
+    fn.__doc__ = doc
+    globals()[name] = fn
+    __all__.append(name)
+    return fn
+
+
+# ---------------------------------------------------------------- reduction
+# reference bindings.py:441-535
+
+
+def _validate_reduction_input(x: torch.Tensor) -> None:
+    if not x.is_cuda:
+        raise ValueError("reduction input must be a CUDA tensor")
+    if x.ndim != 1:
+        raise ValueError("reduction input must be 1-D")
+    if x.dtype != torch.float32:
+        raise TypeError("reduction currently supports float32 only")
+    if not x.is_contiguous():
+        raise ValueError("reduction input must be contiguous")
+
+
+def _validate_reduction_output(x: torch.Tensor, out: torch.Tensor) -> None:
+    if not out.is_cuda or out.device != x.device:
+        raise ValueError("output must be a CUDA tensor on the same device")
+    if out.dtype != torch.float32 or out.numel() != 1 or not out.is_contiguous():
+        raise ValueError("output must be one contiguous float32 CUDA value")
+
+
+def _make_reduction(version: int) -> None:
+    symbol = f"cuda_operator_reduction_v{version}"
+
+    def into(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        _validate_reduction_input(x)
+        _validate_reduction_output(x, out)
+        _call(symbol, _ptr(x) if x.numel() else ctypes.c_void_p(), _ptr(out),
+              ctypes.c_uint64(x.numel()), _stream(x))
+        return out
+
+    def alloc(x: torch.Tensor) -> torch.Tensor:
+        return into(x, torch.empty(1, device=x.device, dtype=torch.float32))
+
+    doc = (f"Global fp32 sum into a one-element tensor (reference reduction_v{version}); "
+           "fp64 accumulation with a fixed, run-to-run reproducible combine order.")
+    _export(f"reduction_v{version}_into", into, doc)
+    _export(f"reduction_v{version}", alloc, doc)
+
+
+for _v in range(6):
+    _make_reduction(_v)
+
+
+def reduction_partial_f64_into(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """fp64 partial sum of a 1-D fp32 CUDA tensor into a one-element float64 tensor.
+
+    The per-rank step of the multi-GPU reduction: each rank sums its chunk,
+    then an all-reduce of the float64 partials forms the global sum.
+    """
+    _validate_reduction_input(x)
+    if not out.is_cuda or out.device != x.device:
+        raise ValueError("output must be a CUDA tensor on the same device")
+    if out.dtype != torch.float64 or out.numel() != 1 or not out.is_contiguous():
+        raise ValueError("output must be one contiguous float64 CUDA value")
+    _call("cuda_operator_reduction_partial_f64", _ptr(x) if x.numel() else ctypes.c_void_p(),
+          _ptr(out), ctypes.c_uint64(x.numel()), _stream(x))
+    return out
+
+
+def reduction_partial_f64(x: torch.Tensor) -> torch.Tensor:
+    """Allocating form of :func:`reduction_partial_f64_into`."""
+    return reduction_partial_f64_into(x, torch.empty(1, device=x.device, dtype=torch.float64))
+
+
+__all__ += ["reduction_partial_f64_into", "reduction_partial_f64"]
+
+# ---------------------------------------------------------------- softmax
+# reference bindings.py:538-649
+
+
+def _validate_softmax_input(x: torch.Tensor) -> None:
+    if not x.is_cuda:
+        raise ValueError("softmax input must be a CUDA tensor")
+    if x.ndim != 2:
+        raise ValueError("softmax input must be 2-D [rows, cols]")
+    if x.dtype != torch.float32:
+        raise TypeError("softmax currently supports float32 only")
+    if not x.is_contiguous():
+        raise ValueError("softmax input must be contiguous")
+    if x.shape[1] == 0:
+        raise ValueError("softmax requires cols > 0")
+
+
+def _validate_softmax_output(x: torch.Tensor, out: torch.Tensor) -> None:
+    if not out.is_cuda or out.device != x.device:
+        raise ValueError("softmax output must be a CUDA tensor on the same device")
+    if out.dtype != torch.float32 or out.shape != x.shape or not out.is_contiguous():
+        raise ValueError("softmax output must be contiguous float32 with the same shape")
+
+
+def _make_softmax(version: int) -> None:
+    symbol = f"cuda_operator_softmax_v{version}"
+
+    def into(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        _validate_softmax_input(x)
+        _validate_softmax_output(x, out)
+        rows, cols = x.shape
+        if rows == 0:
+            return out
+        _call(symbol, _ptr(x), _ptr(out), ctypes.c_uint64(rows), ctypes.c_uint64(cols), _stream(x))
+        return out
+
+    def alloc(x: torch.Tensor) -> torch.Tensor:
+        return into(x, torch.empty_like(x))
+
+    doc = f"Row-wise fp32 softmax (reference softmax_v{version})."
+    _export(f"softmax_v{version}_into", into, doc)
+    _export(f"softmax_v{version}", alloc, doc)
+
+
+for _v in range(6):
+    _make_softmax(_v)
+
+# ---------------------------------------------------------------- RMSNorm
+# reference bindings.py:652-873
+
+
+def _validate_rmsnorm_input(x: torch.Tensor, weight: torch.Tensor, eps: float,
+                            dtype: torch.dtype = torch.float32) -> None:
+    if not x.is_cuda or not weight.is_cuda:
+        raise ValueError("rmsnorm input and weight must be CUDA tensors")
+    if x.ndim != 2:
+        raise ValueError("rmsnorm input must be 2-D [rows, cols]")
+    if weight.ndim != 1 or weight.shape[0] != x.shape[1]:
+        raise ValueError("rmsnorm weight must be 1-D with length equal to cols")
+    if x.dtype != dtype or weight.dtype != dtype:
+        if dtype == torch.float32:
+            raise TypeError("rmsnorm currently supports float32 only")
+        raise TypeError("rmsnorm_bf16 expects bfloat16 input and weight")
+    if not x.is_contiguous() or not weight.is_contiguous():
+        raise ValueError("rmsnorm input and weight must be contiguous")
+    if x.shape[1] == 0:
+        raise ValueError("rmsnorm requires cols > 0")
+    if eps <= 0:
+        raise ValueError("rmsnorm eps must be positive")
+
+
+def _validate_rmsnorm_output(x: torch.Tensor, out: torch.Tensor) -> None:
+    if not out.is_cuda or out.device != x.device:
+        raise ValueError("rmsnorm output must be a CUDA tensor on the same device")
+    if out.dtype != x.dtype or out.shape != x.shape or not out.is_contiguous():
+        if x.dtype == torch.float32:
+            raise ValueError("rmsnorm output must be contiguous float32 with the same shape")
+        raise ValueError("rmsnorm output must be contiguous bfloat16 with the same shape")
+
+
+def _make_rmsnorm(version: int) -> None:
+    symbol = f"cuda_operator_rmsnorm_v{version}"
+
+    def into(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor,
+             eps: float = 1e-5) -> torch.Tensor:
+        _validate_rmsnorm_input(x, weight, eps)
+        _validate_rmsnorm_output(x, out)
+        rows, cols = x.shape
+        if rows == 0:
+            return out
+        _call(symbol, _ptr(x), _ptr(weight), _ptr(out), ctypes.c_uint64(rows),
+              ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x))
+        return out
+
+    def alloc(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+        return into(x, weight, torch.empty_like(x), eps)
+
+    doc = f"Row-wise fp32 RMSNorm x*rsqrt(mean(x^2)+eps)*w (reference rmsnorm_v{version})."
+    _export(f"rmsnorm_v{version}_into", into, doc)
+    _export(f"rmsnorm_v{version}", alloc, doc)
+
+
+for _v in range(5):
+    _make_rmsnorm(_v)
+
+
+def rmsnorm_bf16_into(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor,
+                      eps: float = 1e-5) -> torch.Tensor:
+    """bf16 RMSNorm with fp32 statistics: out = bf16(x * rsqrt(mean(x^2)+eps) * w)."""
+    _validate_rmsnorm_input(x, weight, eps, torch.bfloat16)
+    _validate_rmsnorm_output(x, out)
+    rows, cols = x.shape
+    if rows == 0:
+        return out
+    _call("cuda_operator_rmsnorm_bf16", _ptr(x), _ptr(weight), _ptr(out), ctypes.c_uint64(rows),
+          ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x))
+    return out
+
+
+def rmsnorm_bf16(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """Allocating form of :func:`rmsnorm_bf16_into`."""
+    return rmsnorm_bf16_into(x, weight, torch.empty_like(x), eps)
+
+
+__all__ += ["rmsnorm_bf16_into", "rmsnorm_bf16"]
+
+# ---------------------------------------------------------------- LayerNorm
+# reference bindings.py:875-1151
+
+
+def _validate_layernorm_input(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                              eps: float) -> None:
+    if not x.is_cuda or not weight.is_cuda or not bias.is_cuda:
+        raise ValueError("layernorm input, weight, and bias must be CUDA tensors")
+    if x.ndim != 2:
+        raise ValueError("layernorm input must be 2-D [rows, cols]")
+    if weight.ndim != 1 or weight.shape[0] != x.shape[1]:
+        raise ValueError("layernorm weight must be 1-D with length equal to cols")
+    if bias.ndim != 1 or bias.shape[0] != x.shape[1]:
+        raise ValueError("layernorm bias must be 1-D with length equal to cols")
+    if x.dtype != torch.float32 or weight.dtype != torch.float32 or bias.dtype != torch.float32:
+        raise TypeError("layernorm currently supports float32 only")
+    if not x.is_contiguous() or not weight.is_contiguous() or not bias.is_contiguous():
+        raise ValueError("layernorm input, weight, and bias must be contiguous")
+    if x.shape[1] == 0:
+        raise ValueError("layernorm requires cols > 0")
+    if eps <= 0:
+        raise ValueError("layernorm eps must be positive")
+
+
+def _validate_layernorm_output(x: torch.Tensor, out: torch.Tensor) -> None:
+    if not out.is_cuda or out.device != x.device:
+        raise ValueError("layernorm output must be a CUDA tensor on the same device")
+    if out.dtype != torch.float32 or out.shape != x.shape or not out.is_contiguous():
+        raise ValueError("layernorm output must be contiguous float32 with the same shape")
+
+
+def _make_layernorm(version: int) -> None:
+    symbol = f"cuda_operator_layernorm_v{version}"
+
+    def into(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, out: torch.Tensor,
+             eps: float = 1e-5) -> torch.Tensor:
+        _validate_layernorm_input(x, weight, bias, eps)
+        _validate_layernorm_output(x, out)
+        rows, cols = x.shape
+        if rows == 0:
+            return out
+        _call(symbol, _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), ctypes.c_uint64(rows),
+              ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x))
+        return out
+
+    def alloc(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+              eps: float = 1e-5) -> torch.Tensor:
+        return into(x, weight, bias, torch.empty_like(x), eps)
+
+    doc = f"Row-wise fp32 LayerNorm, biased variance (reference layernorm_v{version})."
+    _export(f"layernorm_v{version}_into", into, doc)
+    _export(f"layernorm_v{version}", alloc, doc)
+
+
+for _v in range(6):
+    _make_layernorm(_v)
+
+# ---------------------------------------------------------------- residual + LayerNorm
+# reference bindings.py:1154-1391
+
+
+def _validate_fused_residual_layernorm_input(x: torch.Tensor, residual: torch.Tensor,
+                                             weight: torch.Tensor, bias: torch.Tensor,
+                                             eps: float) -> None:
+    if not x.is_cuda or not residual.is_cuda or not weight.is_cuda or not bias.is_cuda:
+        raise ValueError("all fused residual layernorm inputs must be CUDA tensors")
+    if x.ndim != 2 or residual.shape != x.shape:
+        raise ValueError("x and residual must have the same 2-D shape")
+    if weight.ndim != 1 or weight.shape[0] != x.shape[1]:
+        raise ValueError("weight must be 1-D with length equal to cols")
+    if bias.ndim != 1 or bias.shape[0] != x.shape[1]:
+        raise ValueError("bias must be 1-D with length equal to cols")
+    if any(t.dtype != torch.float32 for t in (x, residual, weight, bias)):
+        raise TypeError("fused residual layernorm currently supports float32 only")
+    if not all(t.is_contiguous() for t in (x, residual, weight, bias)):
+        raise ValueError("all fused residual layernorm inputs must be contiguous")
+    if x.shape[1] == 0:
+        raise ValueError("fused residual layernorm requires cols > 0")
+    if eps <= 0:
+        raise ValueError("eps must be positive")
+
+
+def _make_residual_layernorm(version: int) -> None:
+    symbol = f"cuda_operator_fused_residual_layernorm_v{version}"
+
+    def into(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+             out: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+        _validate_fused_residual_layernorm_input(x, residual, weight, bias, eps)
+        _validate_layernorm_output(x, out)
+        rows, cols = x.shape
+        if rows == 0:
+            return out
+        _call(symbol, _ptr(x), _ptr(residual), _ptr(weight), _ptr(bias), _ptr(out),
+              ctypes.c_uint64(rows), ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x))
+        return out
+
+    def alloc(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+              eps: float = 1e-5) -> torch.Tensor:
+        return into(x, residual, weight, bias, torch.empty_like(x), eps)
+
+    doc = (f"LayerNorm(x + residual), fp32; h itself is not stored "
+           f"(reference fused_residual_layernorm_v{version}).")
+    _export(f"fused_residual_layernorm_v{version}_into", into, doc)
+    _export(f"fused_residual_layernorm_v{version}", alloc, doc)
+
+
+for _v in range(5):
+    _make_residual_layernorm(_v)
+
+
+def fused_residual_layernorm_h_into(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                                    bias: torch.Tensor, h_out: torch.Tensor, out: torch.Tensor,
+                                    eps: float = 1e-5) -> tuple[torch.Tensor, torch.Tensor]:
+    """Residual add + LayerNorm in one pass, storing both h = x + residual and LN(h)."""
+    _validate_fused_residual_layernorm_input(x, residual, weight, bias, eps)
+    _validate_layernorm_output(x, out)
+    _validate_layernorm_output(x, h_out)
+    rows, cols = x.shape
+    if rows == 0:
+        return h_out, out
+    _call("cuda_operator_fused_residual_layernorm_h", _ptr(x), _ptr(residual), _ptr(weight),
+          _ptr(bias), _ptr(h_out), _ptr(out), ctypes.c_uint64(rows), ctypes.c_uint64(cols),
+          ctypes.c_float(eps), _stream(x))
+    return h_out, out
+
+
+def fused_residual_layernorm_h(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                               bias: torch.Tensor,
+                               eps: float = 1e-5) -> tuple[torch.Tensor, torch.Tensor]:
+    """Allocating form of :func:`fused_residual_layernorm_h_into`; returns (h, y)."""
+    return fused_residual_layernorm_h_into(x, residual, weight, bias, torch.empty_like(x),
+                                           torch.empty_like(x), eps)
+
+
+__all__ += ["fused_residual_layernorm_h_into", "fused_residual_layernorm_h"]
+
+# ---------------------------------------------------------------- bias + GELU
+# reference bindings.py:1394-1523
+
+
+def _make_bias_gelu(version: int) -> None:
+    symbol = f"cuda_operator_fused_bias_gelu_v{version}"
+
+    def into(x: torch.Tensor, bias: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        if not x.is_cuda or not bias.is_cuda or not out.is_cuda:
+            raise ValueError("fused bias GELU tensors must be CUDA tensors")
+        if x.ndim != 2 or bias.ndim != 1 or bias.shape[0] != x.shape[1]:
+            raise ValueError("expected x[rows, cols] and bias[cols]")
+        if x.dtype != torch.float32 or bias.dtype != torch.float32 or out.dtype != torch.float32:
+            raise TypeError("fused bias GELU currently supports float32 only")
+        if out.shape != x.shape:
+            raise ValueError("output shape must equal input shape")
+        if not x.is_contiguous() or not bias.is_contiguous() or not out.is_contiguous():
+            raise ValueError("all tensors must be contiguous")
+        if x.shape[1] == 0:
+            raise ValueError("cols must be > 0")
+        rows, cols = x.shape
+        if rows == 0:
+            return out
+        _call(symbol, _ptr(x), _ptr(bias), _ptr(out), ctypes.c_uint64(rows),
+              ctypes.c_uint64(cols), _stream(x))
+        return out
+
+    def alloc(x: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+        return into(x, bias, torch.empty_like(x))
+
+    doc = f"gelu_erf(x + bias[col]), fp32 (reference fused_bias_gelu_v{version})."
+    _export(f"fused_bias_gelu_v{version}_into", into, doc)
+    _export(f"fused_bias_gelu_v{version}", alloc, doc)
+
+
+for _v in range(3):
+    _make_bias_gelu(_v)
+
+# ---------------------------------------------------------------- SwiGLU
+# reference bindings.py:1526-1641
+
+
+def _validate_swiglu(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor) -> None:
+    if not gate.is_cuda or not up.is_cuda or not out.is_cuda:
+        raise ValueError("SwiGLU tensors must be CUDA tensors")
+    if gate.shape != up.shape or out.shape != gate.shape:
+        raise ValueError("gate, up, and output must have the same shape")
+    if gate.dtype != torch.float32 or up.dtype != torch.float32 or out.dtype != torch.float32:
+        raise TypeError("SwiGLU currently supports float32 only")
+    if not gate.is_contiguous() or not up.is_contiguous() or not out.is_contiguous():
+        raise ValueError("SwiGLU tensors must be contiguous")
+
+
+def _make_swiglu(version: int) -> None:
+    symbol = f"cuda_operator_swiglu_v{version}"
+
+    def into(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        _validate_swiglu(gate, up, out)
+        if version == 2:
+            if gate.ndim != 2:
+                raise ValueError("SwiGLU V2 expects a 2-D tensor")
+            rows, cols = gate.shape
+            if rows == 0:
+                return out
+            _call(symbol, _ptr(gate), _ptr(up), _ptr(out), ctypes.c_uint64(rows),
+                  ctypes.c_uint64(cols), _stream(gate))
+            return out
+        if gate.numel() == 0:
+            return out
+        _call(symbol, _ptr(gate), _ptr(up), _ptr(out), ctypes.c_uint64(gate.numel()),
+              _stream(gate))
+        return out
+
+    def alloc(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+        return into(gate, up, torch.empty_like(gate))
+
+    doc = f"silu(gate) * up, fp32 (reference swiglu_v{version})."
+    _export(f"swiglu_v{version}_into", into, doc)
+    _export(f"swiglu_v{version}", alloc, doc)
+
+
+for _v in range(3):
+    _make_swiglu(_v)
+
+# ---------------------------------------------------------------- GEMM + bias + GELU
+# reference bindings.py:1644-2033
+
+
+def _make_gemm_bias_gelu(version: int) -> None:
+    symbol = f"cuda_operator_gemm_bias_gelu_v{version}"
+
+    def into(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+             out: torch.Tensor) -> torch.Tensor:
+        if not all(t.is_cuda for t in (x, weight, bias, out)):
+            raise ValueError("GEMM Bias GELU tensors must be CUDA tensors")
+        if x.ndim != 2 or weight.ndim != 2:
+            raise ValueError("x and weight must be 2-D")
+        if x.shape[1] != weight.shape[1]:
+            raise ValueError("x.shape[1] must equal weight.shape[1]")
+        if bias.ndim != 1 or bias.shape[0] != weight.shape[0]:
+            raise ValueError("bias length must equal weight.shape[0]")
+        expected_shape = (x.shape[0], weight.shape[0])
+        if out.shape != expected_shape:
+            raise ValueError(f"output shape must be {expected_shape}")
+        if any(t.dtype != torch.float32 for t in (x, weight, bias, out)):
+            raise TypeError("GEMM Bias GELU currently supports float32 only")
+        if not all(t.is_contiguous() for t in (x, weight, bias, out)):
+            raise ValueError("all GEMM Bias GELU tensors must be contiguous")
+        m, k = x.shape
+        n = weight.shape[0]
+        if m == 0 or n == 0:
+            return out
+        _call(symbol, _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), ctypes.c_uint64(m),
+              ctypes.c_uint64(k), ctypes.c_uint64(n), _stream(x))
+        return out
+
+    def alloc(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+        out = torch.empty((x.shape[0], weight.shape[0]), device=x.device, dtype=torch.float32)
+        return into(x, weight, bias, out)
+
+    form = "erf" if version <= 1 else "tanh"
+    doc = f"gelu_{form}(x @ weight.T + bias), fp32 (reference gemm_bias_gelu_v{version})."
+    _export(f"gemm_bias_gelu_v{version}_into", into, doc)
+    _export(f"gemm_bias_gelu_v{version}", alloc, doc)
+
+
+for _v in range(7):
+    _make_gemm_bias_gelu(_v)
+
+
+def gemm_bias_gelu_bf16_into(x_bf16: torch.Tensor, weight_bf16: torch.Tensor, bias: torch.Tensor,
+                             out_bf16: torch.Tensor) -> torch.Tensor:
+    """bf16 tensor-core gelu_erf(x @ W.T + bias) with fp32 accumulation and bf16 output."""
+    if not all(t.is_cuda for t in (x_bf16, weight_bf16, bias, out_bf16)):
+        raise ValueError("GEMM Bias GELU tensors must be CUDA tensors")
+    if x_bf16.ndim != 2 or weight_bf16.ndim != 2:
+        raise ValueError("x and weight must be 2-D")
+    if x_bf16.shape[1] != weight_bf16.shape[1]:
+        raise ValueError("x.shape[1] must equal weight.shape[1]")
+    if bias.ndim != 1 or bias.shape[0] != weight_bf16.shape[0]:
+        raise ValueError("bias length must equal weight.shape[0]")
+    expected_shape = (x_bf16.shape[0], weight_bf16.shape[0])
+    if out_bf16.shape != expected_shape:
+        raise ValueError(f"output shape must be {expected_shape}")
+    if any(t.dtype != torch.bfloat16 for t in (x_bf16, weight_bf16, out_bf16)):
+        raise TypeError("GEMM Bias GELU bf16 expects bfloat16 x, weight and output")
+    if bias.dtype != torch.float32:
+        raise TypeError("GEMM Bias GELU bf16 expects a float32 bias")
+    if not all(t.is_contiguous() for t in (x_bf16, weight_bf16, bias, out_bf16)):
+        raise ValueError("all GEMM Bias GELU tensors must be contiguous")
+    m, k = x_bf16.shape
+    n = weight_bf16.shape[0]
+    if m == 0 or n == 0:
+        return out_bf16
+    _call("cuda_operator_gemm_bias_gelu_bf16", _ptr(x_bf16), _ptr(weight_bf16), _ptr(bias),
+          _ptr(out_bf16), ctypes.c_uint64(m), ctypes.c_uint64(k), ctypes.c_uint64(n),
+          _stream(x_bf16))
+    return out_bf16
+
+
+def gemm_bias_gelu_bf16(x_bf16: torch.Tensor, weight_bf16: torch.Tensor,
+                        bias: torch.Tensor) -> torch.Tensor:
+    """Allocating form of :func:`gemm_bias_gelu_bf16_into`."""
+    out = torch.empty((x_bf16.shape[0], weight_bf16.shape[0]), device=x_bf16.device,
+                      dtype=torch.bfloat16)
+    return gemm_bias_gelu_bf16_into(x_bf16, weight_bf16, bias, out)
+
+
+__all__ += ["gemm_bias_gelu_bf16_into", "gemm_bias_gelu_bf16"]
+
+# ---------------------------------------------------------------- GEMM + SwiGLU
+# reference bindings.py:2036-2818
+
+
+def _make_gemm_swiglu_f32_dual(version: int) -> None:
+    """v0/v1: fp32 X, separate gate/up weights, fp32 workspace and output."""
+    symbol = f"cuda_operator_gemm_swiglu_v{version}"
+
+    def into(x: torch.Tensor, gate_weight: torch.Tensor, up_weight: torch.Tensor,
+             workspace: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        if not all(t.is_cuda for t in (x, gate_weight, up_weight, workspace, out)):
+            raise ValueError("GEMM SwiGLU tensors must be CUDA tensors")
+        if x.ndim != 2 or gate_weight.ndim != 2 or up_weight.ndim != 2:
+            raise ValueError("x and weights must be 2-D")
+        if gate_weight.shape != up_weight.shape:
+            raise ValueError("gate_weight and up_weight must have the same shape")
+        if x.shape[1] != gate_weight.shape[1]:
+            raise ValueError("x.shape[1] must equal weight.shape[1]")
+        expected_shape = (x.shape[0], gate_weight.shape[0])
+        if workspace.shape != expected_shape or out.shape != expected_shape:
+            raise ValueError(f"workspace and output shape must be {expected_shape}")
+        if any(t.dtype != torch.float32 for t in (x, gate_weight, up_weight, workspace, out)):
+            raise TypeError("GEMM SwiGLU currently supports float32 only")
+        if not all(t.is_contiguous() for t in (x, gate_weight, up_weight, workspace, out)):
+            raise ValueError("all GEMM SwiGLU tensors must be contiguous")
+        m, k = x.shape
+        n = gate_weight.shape[0]
+        if m == 0 or n == 0:
+            return out
+        if workspace.data_ptr() == out.data_ptr():
+            raise ValueError("workspace and output must not alias")
+        _call(symbol, _ptr(x), _ptr(gate_weight), _ptr(up_weight), _ptr(workspace), _ptr(out),
+              ctypes.c_uint64(m), ctypes.c_uint64(k), ctypes.c_uint64(n), _stream(x))
+        return out
+
+    def alloc(x: torch.Tensor, gate_weight: torch.Tensor, up_weight: torch.Tensor) -> torch.Tensor:
+        shape = (x.shape[0], gate_weight.shape[0])
+        workspace = torch.empty(shape, device=x.device, dtype=torch.float32)
+        out = torch.empty(shape, device=x.device, dtype=torch.float32)
+        return into(x, gate_weight, up_weight, workspace, out)
+
+    doc = f"silu(x @ Wg.T) * (x @ Wu.T), fp32 (reference gemm_swiglu_v{version})."
+    _export(f"gemm_swiglu_v{version}_into", into, doc)
+    _export(f"gemm_swiglu_v{version}", alloc, doc)
+
+
+def _make_gemm_swiglu_packed(version: int, in_dtype: torch.dtype, ws_dtype: torch.dtype,
+                             doc: str) -> None:
+    """v2/v3 (fp32), v4/v10/v11 (bf16, fp32 workspace), v5 (bf16 workspace)."""
+    symbol = f"cuda_operator_gemm_swiglu_v{version}"
+    tag = f"V{version}"
+    bf16 = in_dtype == torch.bfloat16
+
+    def into(x: torch.Tensor, packed_weight: torch.Tensor, workspace: torch.Tensor,
+             out: torch.Tensor) -> torch.Tensor:
+        if not all(t.is_cuda for t in (x, packed_weight, workspace, out)):
+            raise ValueError(f"GEMM SwiGLU {tag} tensors must be CUDA tensors")
+        if x.ndim != 2 or packed_weight.ndim != 2:
+            raise ValueError("x_bf16 and packed_weight_bf16 must be 2-D" if bf16
+                             else "x and packed_weight must be 2-D")
+        if x.shape[1] != packed_weight.shape[1]:
+            if version in (4, 5):
+                raise ValueError("x_bf16.shape[1] must equal packed_weight_bf16.shape[1]")
+            if version in (10, 11):
+                raise ValueError("x.shape[1] must equal packed_weight.shape[1]")
+            raise ValueError("x.shape[1] must equal packed_weight.shape[1]")
+        if packed_weight.shape[0] % 2 != 0:
+            raise ValueError("packed_weight_bf16.shape[0] must be even" if version in (4, 5)
+                             else "packed_weight.shape[0] must be even")
+        if bf16:
+            if x.dtype != torch.bfloat16 or packed_weight.dtype != torch.bfloat16:
+                raise TypeError(f"GEMM SwiGLU {tag} expects BF16 input and packed weight")
+            if version == 5:
+                if workspace.dtype != torch.bfloat16:
+                    raise TypeError("GEMM SwiGLU V5 workspace must be BF16")
+                if out.dtype != torch.float32:
+                    raise TypeError("GEMM SwiGLU V5 output must be float32")
+            elif workspace.dtype != torch.float32 or out.dtype != torch.float32:
+                if version == 4:
+                    raise TypeError("GEMM SwiGLU V4 workspace and output must be float32")
+                raise TypeError(f"GEMM SwiGLU {tag} workspace/output must be float32")
+        n = packed_weight.shape[0] // 2
+        expected_workspace = (x.shape[0], 2 * n)
+        expected_out = (x.shape[0], n)
+        if workspace.shape != expected_workspace:
+            raise ValueError(f"workspace shape must be {expected_workspace}")
+        if out.shape != expected_out:
+            raise ValueError(f"output shape must be {expected_out}")
+        if not bf16 and any(t.dtype != torch.float32 for t in (x, packed_weight, workspace, out)):
+            raise TypeError(f"GEMM SwiGLU {tag} currently supports float32 only")
+        if not all(t.is_contiguous() for t in (x, packed_weight, workspace, out)):
+            raise ValueError(f"all GEMM SwiGLU {tag} tensors must be contiguous")
+        m, k = x.shape
+        if m == 0 or n == 0:
+            return out
+        _call(symbol, _ptr(x), _ptr(packed_weight), _ptr(workspace), _ptr(out),
+              ctypes.c_uint64(m), ctypes.c_uint64(k), ctypes.c_uint64(n), _stream(x))
+        return out
+
+    def alloc(x: torch.Tensor, packed_weight: torch.Tensor) -> torch.Tensor:
+        n = packed_weight.shape[0] // 2
+        workspace = torch.empty((x.shape[0], 2 * n), device=x.device, dtype=ws_dtype)
+        out = torch.empty((x.shape[0], n), device=x.device, dtype=torch.float32)
+        return into(x, packed_weight, workspace, out)
+
+    _export(f"gemm_swiglu_v{version}_into", into, doc)
+    _export(f"gemm_swiglu_v{version}", alloc, doc)
+
+
+_BF16_DUAL_GUARDS = {
+    6: ((16, 16, 16), "GEMM SwiGLU V6 requires M, K, and N to be multiples of 16"),
+    7: ((16, 16, 64), "GEMM SwiGLU V7 requires M and K multiples of 16 and N multiple of 64"),
+    8: ((32, 16, 64),
+        "GEMM SwiGLU V8 requires M multiple of 32, K multiple of 16, and N multiple of 64"),
+    9: ((16, 16, 128), "GEMM SwiGLU V9 requires M,K multiples of 16 and N multiple of 128"),
+}
+
+
+def _make_gemm_swiglu_bf16_dual(version: int) -> None:
+    """v6..v9: bf16 X, separate bf16 gate/up weights, fp32 output, shape guards."""
+    symbol = f"cuda_operator_gemm_swiglu_v{version}"
+    tag = f"V{version}"
+    (m_mult, k_mult, n_mult), guard_message = _BF16_DUAL_GUARDS[version]
+
+    def into(x_bf16: torch.Tensor, gate_weight_bf16: torch.Tensor, up_weight_bf16: torch.Tensor,
+             out: torch.Tensor) -> torch.Tensor:
+        tensors = (x_bf16, gate_weight_bf16, up_weight_bf16, out)
+        if not all(t.is_cuda for t in tensors):
+            raise ValueError(f"GEMM SwiGLU {tag} tensors must be CUDA tensors")
+        if x_bf16.ndim != 2 or gate_weight_bf16.ndim != 2 or up_weight_bf16.ndim != 2:
+            raise ValueError("x and weights must be 2-D")
+        if gate_weight_bf16.shape != up_weight_bf16.shape:
+            raise ValueError("gate and up weights must have the same shape")
+        if x_bf16.shape[1] != gate_weight_bf16.shape[1]:
+            raise ValueError("x.shape[1] must equal weight.shape[1]")
+        if any(t.dtype != torch.bfloat16 for t in (x_bf16, gate_weight_bf16, up_weight_bf16)):
+            raise TypeError(f"GEMM SwiGLU {tag} expects BF16 input and weights")
+        if out.dtype != torch.float32:
+            raise TypeError(f"GEMM SwiGLU {tag} output must be float32")
+        expected_out = (x_bf16.shape[0], gate_weight_bf16.shape[0])
+        if out.shape != expected_out:
+            raise ValueError(f"output shape must be {expected_out}")
+        if not all(t.is_contiguous() for t in tensors):
+            raise ValueError(f"all GEMM SwiGLU {tag} tensors must be contiguous")
+        m, k = x_bf16.shape
+        n = gate_weight_bf16.shape[0]
+        if m == 0 or n == 0:
+            return out
+        if (m % m_mult) != 0 or (k % k_mult) != 0 or (n % n_mult) != 0:
+            raise ValueError(guard_message)
+        _call(symbol, _ptr(x_bf16), _ptr(gate_weight_bf16), _ptr(up_weight_bf16), _ptr(out),
+              ctypes.c_uint64(m), ctypes.c_uint64(k), ctypes.c_uint64(n), _stream(x_bf16))
+        return out
+
+    def alloc(x_bf16: torch.Tensor, gate_weight_bf16: torch.Tensor,
+              up_weight_bf16: torch.Tensor) -> torch.Tensor:
+        out = torch.empty((x_bf16.shape[0], gate_weight_bf16.shape[0]), device=x_bf16.device,
+                          dtype=torch.float32)
+        return into(x_bf16, gate_weight_bf16, up_weight_bf16, out)
+
+    doc = (f"silu(x @ Wg.T) * (x @ Wu.T) from bf16 operands, fp32 accumulate and output "
+           f"(reference gemm_swiglu_v{version}).")
+    _export(f"gemm_swiglu_v{version}_into", into, doc)
+    _export(f"gemm_swiglu_v{version}", alloc, doc)
+
+
+for _v in (0, 1):
+    _make_gemm_swiglu_f32_dual(_v)
+for _v in (2, 3):
+    _make_gemm_swiglu_packed(_v, torch.float32, torch.float32,
+                             f"Packed fp32 GEMM+SwiGLU (reference gemm_swiglu_v{_v}).")
+for _v in (4, 10, 11):
+    _make_gemm_swiglu_packed(
+        _v, torch.bfloat16, torch.float32,
+        f"Packed bf16 GEMM+SwiGLU on tcgen05 tensor cores, fp32 accumulate and output "
+        f"(reference gemm_swiglu_v{_v}); the workspace is validated but not used.")
+_make_gemm_swiglu_packed(
+    5, torch.bfloat16, torch.bfloat16,
+    "Packed bf16 GEMM+SwiGLU whose gate/up projections are rounded to bf16 before SiLU "
+    "(reference gemm_swiglu_v5); the workspace is validated but not used.")
+for _v in (6, 7, 8, 9):
+    _make_gemm_swiglu_bf16_dual(_v)
+
+
+def gemm_swiglu_bf16_into(x_bf16: torch.Tensor, packed_weight_bf16: torch.Tensor,
+                          out_bf16: torch.Tensor) -> torch.Tensor:
+    """Packed bf16 GEMM+SwiGLU with bf16 output: bf16(silu(x@Wg.T) * (x@Wu.T)).
+
+    packed_weight_bf16 is [2N, K] with the N gate rows first.  No workspace:
+    both projections stay in tensor memory until the fused epilogue.
+    """
+    tensors = (x_bf16, packed_weight_bf16, out_bf16)
+    if not all(t.is_cuda for t in tensors):
+        raise ValueError("GEMM SwiGLU bf16 tensors must be CUDA tensors")
+    if x_bf16.ndim != 2 or packed_weight_bf16.ndim != 2:
+        raise ValueError("x_bf16 and packed_weight_bf16 must be 2-D")
+    if x_bf16.shape[1] != packed_weight_bf16.shape[1]:
+        raise ValueError("x_bf16.shape[1] must equal packed_weight_bf16.shape[1]")
+    if packed_weight_bf16.shape[0] % 2 != 0:
+        raise ValueError("packed_weight_bf16.shape[0] must be even")
+    if any(t.dtype != torch.bfloat16 for t in tensors):
+        raise TypeError("GEMM SwiGLU bf16 expects bfloat16 input, packed weight and output")
+    n = packed_weight_bf16.shape[0] // 2
+    expected_out = (x_bf16.shape[0], n)
+    if out_bf16.shape != expected_out:
+        raise ValueError(f"output shape must be {expected_out}")
+    if not all(t.is_contiguous() for t in tensors):
+        raise ValueError("all GEMM SwiGLU bf16 tensors must be contiguous")
+    m, k = x_bf16.shape
+    if m == 0 or n == 0:
+        return out_bf16
+    _call("cuda_operator_gemm_swiglu_bf16", _ptr(x_bf16), _ptr(packed_weight_bf16), _ptr(out_bf16),
+          ctypes.c_uint64(m), ctypes.c_uint64(k), ctypes.c_uint64(n), _stream(x_bf16))
+    return out_bf16
+
+
+def gemm_swiglu_bf16(x_bf16: torch.Tensor, packed_weight_bf16: torch.Tensor) -> torch.Tensor:
+    """Allocating form of :func:`gemm_swiglu_bf16_into`."""
+    out = torch.empty((x_bf16.shape[0], packed_weight_bf16.shape[0] // 2), device=x_bf16.device,
+                      dtype=torch.bfloat16)
+    return gemm_swiglu_bf16_into(x_bf16, packed_weight_bf16, out)
+
+
+__all__ += ["gemm_swiglu_bf16_into", "gemm_swiglu_bf16"]
+
+# ---------------------------------------------------------------- library info
+
+
+def gemm_status(clear: bool = True) -> int:
+    """Bounded-wait status word of the tensor-core GEMM on the current device.
+
+    0 means no mbarrier wait ever ran out of time.  Synchronises the device.
+    """
+    value = ctypes.c_uint(0)
+    _call("cuda_operator_lab_gemm_status", ctypes.byref(value), ctypes.c_int(1 if clear else 0))
+    return int(value.value)
+
+
+def device_info() -> dict[str, int]:
+    """SM count and compute capability of the current device, as the library sees them."""
+    sm, major, minor = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    _call("cuda_operator_lab_device_info", ctypes.byref(sm), ctypes.byref(major),
+          ctypes.byref(minor))
+    return {"sm_count": sm.value, "cc_major": major.value, "cc_minor": minor.value}
+
+
+def build_tag() -> str:
+    """Build tag string compiled into the loaded library."""
+    return _library().handle.cuda_operator_lab_build_tag().decode()
+
+
+__all__ += ["gemm_status", "device_info", "build_tag", "library_path", "REFERENCE_SYMBOLS"]

@@ -1,0 +1,203 @@
+"""Parity of the GEMM epilogue kernels with the CPU oracle (GPU).
+
+bf16 operands run on the tcgen05 tensor-core kernel (TMA-addressable shapes)
+or the CUDA-core kernel (K not a multiple of 8); fp32 operands run on the
+CUDA-core kernel.  Tolerances: bf16 epilogues rtol 2e-2 / atol 2e-2 against
+the fp32-accumulated reference (BASELINE), fp32 epilogues rtol/atol 3e-4
+(reference tests/test_gemm_bias_gelu_v0.py).  Shapes follow the reference's
+tests (tests/test_gemm_swiglu_v4.py:16-28, test_gemm_swiglu_v11.py:19-31)
+plus tile-boundary and BASELINE shapes.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import seeded
+from cuda_operator_lab import bindings as b
+from oracle import reference_math as oracle
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+BF_RTOL, BF_ATOL = 2e-2, 2e-2
+F32_TOL = 3e-4
+
+
+@pytest.fixture(autouse=True)
+def no_wait_timeouts():
+    b.gemm_status(clear=True)
+    yield
+    assert b.gemm_status(clear=True) == 0, "a bounded mbarrier wait timed out"
+
+
+def bf16_inputs(m, k, n, seed, scale=None):
+    g = seeded(seed)
+    s = scale if scale is not None else k ** -0.5
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    wg = (torch.randn(n, k, generator=g) * s).to(torch.bfloat16)
+    wu = (torch.randn(n, k, generator=g) * s).to(torch.bfloat16)
+    return x, wg, wu
+
+
+def close(actual, expected, rtol, atol):
+    torch.cuda.synchronize()
+    torch.testing.assert_close(actual.cpu().float(), expected.float(), rtol=rtol, atol=atol)
+
+
+BF16_SHAPES = [
+    (1, 8, 1), (4, 16, 32), (16, 64, 64), (17, 40, 24), (32, 128, 256), (64, 256, 512),
+    (128, 64, 2048), (128, 512, 1024), (129, 72, 130), (200, 136, 300), (128, 1024, 4096),
+    (512, 1024, 4096), (384, 4096, 256), (1000, 520, 700),
+]
+
+
+@pytest.mark.parametrize("version", [4, 10, 11])
+@pytest.mark.parametrize(("m", "k", "n"), BF16_SHAPES)
+def test_packed_bf16_swiglu_fp32_out(version, m, k, n):
+    x, wg, wu = bf16_inputs(m, k, n, 20261025 + m * 1000000 + k * 1000 + n)
+    packed = torch.cat((wg, wu), dim=0).contiguous()
+    fn = getattr(b, f"gemm_swiglu_v{version}")
+    actual = fn(x.to(DEV), packed.to(DEV))
+    close(actual, oracle.gemm_swiglu_bf16_fp32_reference(x, packed), BF_RTOL, BF_ATOL)
+
+
+@pytest.mark.parametrize(("m", "k", "n"), [(1, 1, 1), (4, 16, 32), (17, 31, 63), (33, 100, 70)])
+def test_packed_bf16_swiglu_unaddressable_k_uses_cuda_cores(m, k, n):
+    x, wg, wu = bf16_inputs(m, k, n, 20261026 + m + k + n)
+    packed = torch.cat((wg, wu), dim=0).contiguous()
+    close(b.gemm_swiglu_v4(x.to(DEV), packed.to(DEV)),
+          oracle.gemm_swiglu_bf16_fp32_reference(x, packed), BF_RTOL, BF_ATOL)
+
+
+@pytest.mark.parametrize(("m", "k", "n"), [(16, 64, 64), (32, 128, 256), (256, 512, 384),
+                                           (128, 1024, 4096)])
+def test_packed_bf16_swiglu_bf16_workspace_semantics(m, k, n):
+    x, wg, wu = bf16_inputs(m, k, n, 20261027 + m + k + n)
+    packed = torch.cat((wg, wu), dim=0).contiguous()
+    close(b.gemm_swiglu_v5(x.to(DEV), packed.to(DEV)),
+          oracle.gemm_swiglu_bf16_workspace_reference(x, packed), 1e-2, 1e-1)
+
+
+@pytest.mark.parametrize(("version", "m", "k", "n"), [
+    (6, 16, 16, 64), (6, 32, 128, 256), (6, 48, 80, 16), (7, 16, 16, 64), (7, 128, 512, 1024),
+    (8, 32, 64, 128), (8, 64, 256, 512), (9, 16, 16, 128), (9, 128, 1024, 4096)])
+def test_dual_bf16_swiglu(version, m, k, n):
+    x, wg, wu = bf16_inputs(m, k, n, 20261019 + m * 1000000 + k * 1000 + n, scale=1.0)
+    fn = getattr(b, f"gemm_swiglu_v{version}")
+    actual = fn(x.to(DEV), wg.to(DEV), wu.to(DEV))
+    # unit-variance weights as in the reference tests: values grow with sqrt(k)
+    close(actual, oracle.gemm_swiglu_bf16_dual_fp32_reference(x, wg, wu), 5e-3, 5e-2 * (k ** 0.5))
+
+
+@pytest.mark.parametrize(("version", "m", "k", "n"), [(6, 17, 32, 64), (7, 32, 33, 64),
+                                                      (8, 16, 16, 64), (9, 16, 16, 64)])
+def test_dual_bf16_swiglu_shape_guards(version, m, k, n):
+    x, wg, wu = bf16_inputs(m, k, n, 1)
+    with pytest.raises(ValueError):
+        getattr(b, f"gemm_swiglu_v{version}")(x.to(DEV), wg.to(DEV), wu.to(DEV))
+
+
+@pytest.mark.parametrize(("m", "k", "n"), [(1, 8, 1), (16, 64, 64), (100, 256, 300),
+                                           (128, 64, 2048), (512, 4096, 4096), (1000, 1024, 1500)])
+def test_gemm_swiglu_bf16_output(m, k, n):
+    x, wg, wu = bf16_inputs(m, k, n, 20261201 + m + k + n)
+    packed = torch.cat((wg, wu), dim=0).contiguous()
+    actual = b.gemm_swiglu_bf16(x.to(DEV), packed.to(DEV))
+    assert actual.dtype == torch.bfloat16
+    close(actual, oracle.gemm_swiglu_bf16_fp32_reference(x, packed), BF_RTOL, BF_ATOL)
+
+
+@pytest.mark.parametrize(("m", "k", "n"), [(1, 8, 1), (16, 64, 64), (100, 256, 300),
+                                           (512, 4096, 4096), (257, 520, 1000), (3, 30, 5)])
+def test_gemm_bias_gelu_bf16(m, k, n):
+    g = seeded(20261202 + m + k + n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * k ** -0.5).to(torch.bfloat16)
+    bias = torch.randn(n, generator=g) * 0.1
+    actual = b.gemm_bias_gelu_bf16(x.to(DEV), w.to(DEV), bias.to(DEV))
+    close(actual, oracle.gemm_bias_gelu(x.float(), w.float(), bias), BF_RTOL, BF_ATOL)
+
+
+FP32_SHAPES = [(1, 1, 1), (1, 7, 13), (4, 16, 32), (17, 31, 63), (32, 128, 256), (64, 256, 512),
+               (128, 512, 1024)]
+
+
+@pytest.mark.parametrize("version", range(7))
+@pytest.mark.parametrize(("m", "k", "n"), FP32_SHAPES)
+def test_fp32_gemm_bias_gelu(version, m, k, n):
+    g = seeded(20261005 + m * 1000000 + k * 1000 + n)
+    x = torch.randn(m, k, generator=g)
+    w = torch.randn(n, k, generator=g)
+    bias = torch.randn(n, generator=g)
+    fn = getattr(b, f"gemm_bias_gelu_v{version}")
+    ref = oracle.gemm_bias_gelu if version <= 1 else oracle.gemm_bias_gelu_tanh
+    close(fn(x.to(DEV), w.to(DEV), bias.to(DEV)), ref(x, w, bias), F32_TOL, F32_TOL)
+
+
+@pytest.mark.parametrize("version", range(4))
+@pytest.mark.parametrize(("m", "k", "n"), FP32_SHAPES[:-1])
+def test_fp32_gemm_swiglu(version, m, k, n):
+    g = seeded(20261010 + m * 1000000 + k * 1000 + n)
+    x = torch.randn(m, k, generator=g)
+    wg = torch.randn(n, k, generator=g)
+    wu = torch.randn(n, k, generator=g)
+    fn = getattr(b, f"gemm_swiglu_v{version}")
+    if version <= 1:
+        actual = fn(x.to(DEV), wg.to(DEV), wu.to(DEV))
+    else:
+        actual = fn(x.to(DEV), torch.cat((wg, wu), 0).to(DEV))
+    expected = oracle.gemm_swiglu(x, wg, wu)
+    close(actual, expected, F32_TOL, F32_TOL * max(1.0, float(expected.abs().max()) / 100))
+
+
+def test_gemm_golden_cases(golden):
+    seen = 0
+    for case in golden:
+        args = [a.to(DEV) for a in case["args"]]
+        fn = case["fn"]
+        if fn == "gemm_swiglu_bf16_fp32_reference":
+            actual, tol = b.gemm_swiglu_v11(*args), (BF_RTOL, BF_ATOL)
+        elif fn == "gemm_swiglu_bf16_dual_fp32_reference":
+            x, wg, wu = args
+            actual, tol = b.gemm_swiglu_v10(x, torch.cat((wg, wu), 0)), (BF_RTOL, BF_ATOL)
+        elif fn == "gemm_swiglu_bf16_workspace_reference":
+            actual, tol = b.gemm_swiglu_v5(*args), (1e-2, 1e-1)
+        elif fn == "gemm_bias_gelu":
+            actual, tol = b.gemm_bias_gelu_v0(*args), (F32_TOL, F32_TOL)
+        elif fn == "gemm_bias_gelu_tanh":
+            actual, tol = b.gemm_bias_gelu_v6(*args), (F32_TOL, F32_TOL)
+        elif fn == "gemm_swiglu":
+            actual, tol = b.gemm_swiglu_v1(*args), (F32_TOL, F32_TOL)
+        elif fn == "gemm_swiglu_packed":
+            actual, tol = b.gemm_swiglu_v3(*args), (F32_TOL, F32_TOL)
+        else:
+            continue
+        close(actual, case["expected"], *tol)
+        seen += 1
+    assert seen >= 20
+
+
+def test_tensor_core_path_is_exact_on_integer_inputs():
+    # Small integers are exact in bf16 and their products/sums exact in fp32:
+    # the tensor-core result must equal the CPU result bit for bit.
+    g = seeded(5)
+    m, k, n = 256, 512, 384
+    x = torch.randint(-3, 4, (m, k), generator=g).to(torch.bfloat16)
+    wg = torch.randint(-2, 3, (n, k), generator=g).to(torch.bfloat16)
+    wu = torch.randint(-2, 3, (n, k), generator=g).to(torch.bfloat16)
+    packed = torch.cat((wg, wu), 0).contiguous()
+    gate = x.float() @ wg.float().T
+    up = x.float() @ wu.float().T
+    actual = b.gemm_swiglu_v4(x.to(DEV), packed.to(DEV)).cpu()
+    expected = torch.nn.functional.silu(gate) * up
+    torch.testing.assert_close(actual, expected, rtol=1e-6, atol=1e-5)
+
+
+def test_gemm_repeated_calls_are_bitwise_stable():
+    x, wg, wu = bf16_inputs(512, 1024, 1024, 77)
+    packed = torch.cat((wg, wu), 0).contiguous().to(DEV)
+    xd = x.to(DEV)
+    first = b.gemm_swiglu_bf16(xd, packed)
+    for _ in range(3):
+        assert torch.equal(b.gemm_swiglu_bf16(xd, packed), first)
