@@ -34,7 +34,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -248,7 +247,7 @@ def op_table(d: Dist, pk: dict) -> dict:
     """Every other BASELINE config at N=1 (rank 0), plus the sharded large
     RMSNorm and 2^30 reduction at every N.  Cold = L2 flushed before each rep."""
     from cuda_operator_lab import bindings as b
-    from cuda_operator_lab.benchmarking import L2Flusher
+    from cuda_operator_lab.benchmarking import L2Flusher, measure_batch_us
 
     dev = torch.device("cuda")
     ops: dict = {}
@@ -257,7 +256,7 @@ def op_table(d: Dist, pk: dict) -> dict:
     flush = L2Flusher(dev)
 
     def mem_op(name, fn, nbytes, reps=50):
-        warm = event_median_us(fn, reps)
+        warm = measure_batch_us(fn, warmup=3, repeats=reps)
         cold = event_median_us(fn, reps, flush)
         ops[name] = {"us_warm": round(warm, 3), "us_cold": round(cold, 3),
                      "gbs_cold": round(nbytes / cold / 1e3, 1),
@@ -344,9 +343,12 @@ def op_table(d: Dist, pk: dict) -> dict:
     wsm = randn(4096, 64, scale=0.125).to(torch.bfloat16)
     os_ = torch.empty(128, 2048, device=dev)
     ws_ = torch.empty(128, 4096, device=dev)
-    us = event_median_us(lambda: b.gemm_swiglu_v11_into(xs_, wsm, ws_, os_), 100)
-    ops["gemm_swiglu_bf16_128x64x2048_v11"] = {"us_warm": round(us, 3),
-                                               "tflops": round(2 * 128 * 64 * 4096 / us / 1e6, 2)}
+    us = measure_batch_us(lambda: b.gemm_swiglu_v11_into(xs_, wsm, ws_, os_), warmup=5,
+                          repeats=200)
+    us_single = event_median_us(lambda: b.gemm_swiglu_v11_into(xs_, wsm, ws_, os_), 100)
+    ops["gemm_swiglu_bf16_128x64x2048_v11"] = {
+        "us_back_to_back": round(us, 3), "us_single_call": round(us_single, 3),
+        "tflops": round(2 * 128 * 64 * 4096 / us / 1e6, 2)}
     wg = randn(4096, 4096, scale=4096 ** -0.5).to(torch.bfloat16)
     bg = randn(4096, scale=0.1)
     og = torch.empty(512, 4096, device=dev, dtype=torch.bfloat16)
@@ -526,6 +528,59 @@ def run_reference(args) -> dict:
     }
 
 
+KERNEL_CASES = ("gemm_swiglu_bf16", "gemm_bias_gelu_bf16", "rmsnorm_bf16", "reduction",
+                "rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "bias_gelu_fp32", "swiglu_fp32")
+
+
+def run_kernel_case(spec: str, reps: int) -> None:
+    """Launch one op `reps` times at a given size and exit: the command that
+    profilers (ncu) wrap.  spec = NAME[:d0,d1,...], e.g. gemm_swiglu_bf16:2048,4096,14336."""
+    from cuda_operator_lab import bindings as b
+
+    name, _, dims = spec.partition(":")
+    if name not in KERNEL_CASES:
+        raise SystemExit(f"unknown kernel case {name}; choose from {KERNEL_CASES}")
+    d = [int(v) for v in dims.split(",")] if dims else []
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED)
+    rn = lambda *shape: torch.randn(*shape, device=dev, generator=g)  # noqa: E731
+    if name == "gemm_swiglu_bf16":
+        m, k, n = d or (2048, K, N)
+        x, w = rn(m, k).bfloat16(), (rn(2 * n, k) * k ** -0.5).bfloat16()
+        out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        fn = lambda: b.gemm_swiglu_bf16_into(x, w, out)  # noqa: E731
+    elif name == "gemm_bias_gelu_bf16":
+        m, k, n = d or (512, 4096, 4096)
+        x, w, bias = rn(m, k).bfloat16(), (rn(n, k) * k ** -0.5).bfloat16(), rn(n) * 0.1
+        out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        fn = lambda: b.gemm_bias_gelu_bf16_into(x, w, bias, out)  # noqa: E731
+    elif name == "rmsnorm_bf16":
+        r, c = d or (M, K)
+        x, w = rn(r, c).bfloat16(), (torch.rand(c, device=dev, generator=g) + 0.5).bfloat16()
+        y = torch.empty_like(x)
+        fn = lambda: b.rmsnorm_bf16_into(x, w, y, EPS)  # noqa: E731
+    elif name == "reduction":
+        (n,) = d or (1 << 26,)
+        x = torch.rand(n, device=dev, generator=g) * 2 - 1
+        out = torch.empty(1, device=dev)
+        fn = lambda: b.reduction_v5_into(x, out)  # noqa: E731
+    elif name in ("rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "bias_gelu_fp32",
+                  "swiglu_fp32"):
+        r, c = d or (128, 8192 if name == "rmsnorm_fp32" else 4096)
+        x, w, bias, y = rn(r, c), torch.rand(c, device=dev, generator=g) + 0.5, rn(c) * 0.1, None
+        y = torch.empty_like(x)
+        u = rn(r, c)
+        fn = {"rmsnorm_fp32": lambda: b.rmsnorm_v4_into(x, w, y, EPS),
+              "softmax_fp32": lambda: b.softmax_v5_into(x, y),
+              "layernorm_fp32": lambda: b.layernorm_v5_into(x, w, bias, y),
+              "bias_gelu_fp32": lambda: b.fused_bias_gelu_v2_into(x, bias, y),
+              "swiglu_fp32": lambda: b.swiglu_v2_into(x, u, y)}[name]
+    for _ in range(reps):
+        fn()
+    torch.cuda.synchronize()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__,
                                      formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -536,7 +591,13 @@ def main() -> None:
     parser.add_argument("--cpu-seconds", type=float, default=15.0)
     parser.add_argument("--skip-ops", action="store_true")
     parser.add_argument("--skip-cpu", action="store_true")
+    parser.add_argument("--kernel-case", default=None,
+                        help="run one op only (for profilers): NAME[:dims], see KERNEL_CASES")
+    parser.add_argument("--reps", type=int, default=3)
     args = parser.parse_args()
+    if args.kernel_case:
+        run_kernel_case(args.kernel_case, args.reps)
+        return
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
 

@@ -77,9 +77,12 @@ __device__ __forceinline__ double warp_sum_f64(double v) {
 // silu(x) = x / (1 + exp(-x)), the form of swiglu.cu:11-13.
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 
-// Exact GELU, 0.5 x (1 + erf(x / sqrt 2)) (fused_bias_gelu.cu:12-14).
+// Exact GELU, 0.5 x (1 + erf(x / sqrt 2)) (fused_bias_gelu.cu:12-14),
+// evaluated as 0.5 x erfc(-x / sqrt 2): the same function without the
+// cancellation of 1 + erf(.) for x << 0, where the erf form loses most of
+// its significant bits.
 __device__ __forceinline__ float gelu_erf_f(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+  return 0.5f * x * erfcf(-x * 0.70710678118654752440f);
 }
 
 // tanh-approximate GELU, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))),

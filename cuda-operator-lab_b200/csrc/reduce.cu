@@ -1,32 +1,41 @@
 // Global sum of an fp32 vector (reduction.cuh:8-44).
 //
-// The input is split into G fixed chunks of `per_cta` elements (a multiple of
-// 16384, with G <= 4096); CTA b sums chunk b in fp64 (16-byte streaming loads,
-// four independent vectors in flight per thread), writes its partial to a
-// scratch slot, and the CTA that finishes last adds the G partials in index
-// order.  The partition and the combine order depend only on n, so the result
-// is identical from run to run, unlike the fp32 atomicAdd combine of the
-// reference (reduction.cu:43); and the fp64 accumulation keeps the relative
-// error near 1e-12 even for 2^30 inputs, where an fp32 running sum loses ~1e-6.
+// The input is split into G equal chunks (G <= 8 x SM count, one resident
+// wave); CTA b sums chunk b in fp64 (16-byte streaming loads, four
+// independent vectors in flight per thread), writes its partial to a scratch
+// slot, and the CTA that finishes last adds the G partials in index order.
+// The partition and the combine order depend only on n and the SM count, so
+// the result is identical from run to run on a device model, unlike the fp32
+// atomicAdd combine of the reference (reduction.cu:43); and the fp64
+// accumulation keeps the relative error near 1e-12 even for 2^30 inputs,
+// where an fp32 running sum loses ~1e-6.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
 
 constexpr int kThreads = 256;
-constexpr std::uint64_t kChunkQuantum = 16384;  // elements; multiple of 4*kThreads
-constexpr std::uint64_t kMaxCtas = 4096;
+constexpr int kCtasPerSm = 8;                   // 256-thread CTAs resident per SM
+constexpr std::uint64_t kChunkQuantum = 1024;   // elements: one float4 per thread
+constexpr std::uint64_t kMinChunk = 4096;
 
 struct Plan {
   std::uint64_t per_cta;
   unsigned ctas;
 };
 
+// One wave: at most sm_count * 8 CTAs, every chunk the same size (a multiple
+// of 1024 elements, so chunk starts keep 16-byte alignment), so all CTAs are
+// resident at once and finish together.
 Plan plan_for(std::uint64_t n) {
-  const std::uint64_t quanta = (n + kChunkQuantum - 1) / kChunkQuantum;
-  const std::uint64_t mult = (quanta + kMaxCtas - 1) / kMaxCtas;
+  const std::uint64_t target = static_cast<std::uint64_t>(col::device_info().sm_count) * kCtasPerSm;
+  std::uint64_t per = (n + target - 1) / target;
+  per = (per + kChunkQuantum - 1) / kChunkQuantum * kChunkQuantum;
+  if (per < kMinChunk) per = kMinChunk;
   Plan p;
-  p.per_cta = kChunkQuantum * (mult ? mult : 1);
-  p.ctas = static_cast<unsigned>((n + p.per_cta - 1) / p.per_cta);
+  p.per_cta = per;
+  p.ctas = static_cast<unsigned>((n + per - 1) / per);
   return p;
 }
 
@@ -123,14 +132,49 @@ int launch_sum(const float* x, void* out, std::uint64_t n, cudaStream_t s, doubl
   return static_cast<int>(cudaGetLastError());
 }
 
+// Library-owned stream-ordered memory pool of the current device.  Its
+// release threshold keeps freed blocks mapped, so the per-call scratch
+// allocation below is a cheap pool hit instead of a fresh mapping after
+// every synchronisation (what the default pool, threshold 0, would do).
+cudaError_t scratch_pool(cudaMemPool_t* pool) {
+  constexpr int kMaxDevices = 64;
+  static cudaMemPool_t pools[kMaxDevices] = {};
+  static cudaError_t errors[kMaxDevices] = {};
+  static std::once_flag flags[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::call_once(flags[dev], [dev]() {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t p = nullptr;
+    cudaError_t err = cudaMemPoolCreate(&p, &props);
+    if (err == cudaSuccess) {
+      std::uint64_t keep = ~0ull;
+      err = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    pools[dev] = p;
+    errors[dev] = err;
+  });
+  *pool = pools[dev];
+  return errors[dev];
+}
+
 // Stream-ordered scratch: allocated and freed on the caller's stream, so
 // concurrent calls on different streams never share it.
 template <bool OUT_F64>
 int reduce_with_pool_scratch(const float* x, void* out, std::uint64_t n, cudaStream_t s) {
   const Plan p = plan_for(n);
   const std::size_t bytes = static_cast<std::size_t>(p.ctas) * sizeof(double) + 16;
+  cudaMemPool_t pool = nullptr;
+  cudaError_t st = scratch_pool(&pool);
+  if (st != cudaSuccess) return static_cast<int>(st);
   void* scratch = nullptr;
-  cudaError_t st = cudaMallocAsync(&scratch, bytes, s);
+  st = cudaMallocFromPoolAsync(&scratch, bytes, pool, s);
   if (st != cudaSuccess) return static_cast<int>(st);
   double* partials = static_cast<double*>(scratch);
   unsigned* counter = reinterpret_cast<unsigned*>(partials + p.ctas);

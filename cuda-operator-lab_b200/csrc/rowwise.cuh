@@ -64,6 +64,12 @@ __device__ __forceinline__ void load_param(const T* p, float (&v)[VEC]) {
   }
 }
 
+template <typename T>
+__device__ __forceinline__ float load_param1(const T* p) {
+  if constexpr (std::is_same<T, float>::value) return __ldg(p);
+  else return __bfloat162float(p[0]);
+}
+
 template <typename T, int VEC>
 __device__ __forceinline__ void store_vec(T* p, const float (&v)[VEC]) {
   if constexpr (std::is_same<T, float>::value && VEC == 4) {
@@ -196,12 +202,25 @@ row_kernel(const RowArgs a) {
       }
     }
   } else if constexpr (OP == RowOp::kLayerNorm || OP == RowOp::kResidualLayerNorm) {
+    // Shifted sum: subtracting the row's first element (the same value in
+    // every thread of the row) keeps the partial sums small when the row
+    // carries a large common offset, so the mean keeps its low-order bits.
+    float shift = 0.0f;
+    if (row_ok) {
+      shift = load_param1(static_cast<const T*>(a.x) + base);
+      if constexpr (OP == RowOp::kResidualLayerNorm) {
+        shift += load_param1(static_cast<const T*>(a.residual) + base);
+      }
+    }
     float s = 0.0f;
 #pragma unroll
-    for (int j = 0; j < NV; ++j)
+    for (int j = 0; j < NV; ++j) {
+      if (ok[j]) {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) s += v[j][e];
-    const float mean = group_sum<TPR>(s, sh) * inv_cols;
+        for (int e = 0; e < VEC; ++e) s += v[j][e] - shift;
+      }
+    }
+    const float mean = shift + group_sum<TPR>(s, sh) * inv_cols;
     float q = 0.0f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
@@ -327,9 +346,10 @@ __global__ void __launch_bounds__(kLongThreads) row_kernel_long(const RowArgs a)
     const float rstd = rsqrtf(block_sum_long(s, sh) * inv_cols + a.eps);
     for (std::uint32_t i = threadIdx.x; i < cols; i += kLongThreads) st1(y + i, (in(i) * rstd) * ld1(w + i));
   } else if constexpr (OP == RowOp::kLayerNorm || OP == RowOp::kResidualLayerNorm) {
+    const float shift = in(0);  // shifted sum, as in row_kernel
     float s = 0.0f;
-    for (std::uint32_t i = threadIdx.x; i < cols; i += kLongThreads) s += in(i);
-    const float mean = block_sum_long(s, sh) * inv_cols;
+    for (std::uint32_t i = threadIdx.x; i < cols; i += kLongThreads) s += in(i) - shift;
+    const float mean = shift + block_sum_long(s, sh) * inv_cols;
     float q = 0.0f;
     for (std::uint32_t i = threadIdx.x; i < cols; i += kLongThreads) {
       const float d = in(i) - mean;

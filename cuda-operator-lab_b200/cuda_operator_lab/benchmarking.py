@@ -66,14 +66,37 @@ def summarize(samples: list[float]) -> tuple[float, float, float]:
     return statistics.median(samples), percentile(samples, 0.50), percentile(samples, 0.95)
 
 
+def measure_batch_us(fn: Callable[[], object], *, warmup: int, repeats: int) -> float:
+    """Average device time per call of `repeats` back-to-back calls between
+    one event pair: the steady-state cost when the GPU never idles (host
+    launch overhead is hidden unless the host is slower than the kernels)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(repeats):
+        fn()
+    end.record()
+    end.synchronize()
+    return start.elapsed_time(end) * 1000.0 / repeats
+
+
 class L2Flusher:
-    """Evicts the L2 between samples by writing a buffer of 2x its size."""
+    """Evicts the L2 between samples by reading a buffer of twice its size.
+
+    Reading (not writing) leaves the L2 full of clean lines, so the measured
+    kernel pays only for its own DRAM traffic, not for writing back the
+    flush buffer's dirty lines.
+    """
 
     def __init__(self, device: torch.device | int | None = None) -> None:
         props = torch.cuda.get_device_properties(device if device is not None else 0)
         size = max(2 * int(getattr(props, "L2_cache_size", 0) or 0), 256 << 20)
-        self.buffer = torch.empty(size // 4, dtype=torch.float32,
-                                  device=device if device is not None else "cuda")
+        dev = device if device is not None else "cuda"
+        self.buffer = torch.ones(size // 4, dtype=torch.float32, device=dev)
+        self.sink = torch.empty((), dtype=torch.float32, device=dev)
 
     def __call__(self) -> None:
-        self.buffer.fill_(0.0)
+        torch.sum(self.buffer, out=self.sink)

@@ -43,7 +43,8 @@ extern "C" {
  * combine, so the result is bit-reproducible run to run (the reference's
  * fp32 atomicAdd combine, reduction.cu:43, is not).  input may be NULL only
  * when n == 0, in which case out[0] = 0.  Uses a stream-ordered scratch
- * allocation (cudaMallocAsync) of 8 bytes per 16384 inputs. */
+ * allocation (a library-owned cudaMemPool) of 8 bytes per CTA (at most
+ * 8 x SM count CTAs). */
 int cuda_operator_reduction_v0(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:8  */
 int cuda_operator_reduction_v1(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:14 */
 int cuda_operator_reduction_v2(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:20 */

@@ -35,7 +35,13 @@ def test_bias_gelu_matches_oracle(version, rows, cols):
     x = torch.randn(rows, cols, generator=g) * 2.0
     bias = torch.randn(cols, generator=g) * 0.1
     fn = getattr(b, f"fused_bias_gelu_v{version}")
-    close(fn(x.to(DEV), bias.to(DEV)), oracle.fused_bias_gelu(x, bias))
+    actual = fn(x.to(DEV), bias.to(DEV))
+    # BASELINE bar against the exact function of the fp32 inputs.  PyTorch's
+    # own fp32 CPU GELU is off by up to 1.2e-6 near |z| = 3.5, so against the
+    # reference's CPU path the reference tests' bar (5e-6) applies.
+    exact = torch.nn.functional.gelu((x + bias).double()).float()
+    close(actual, exact)
+    close(actual, oracle.fused_bias_gelu(x, bias), rtol=5e-6, atol=5e-6)
 
 
 @pytest.mark.parametrize("version", range(3))
@@ -69,11 +75,12 @@ def test_pointwise_golden_cases(golden):
         args = [a.to(DEV) for a in case["args"]]
         if case["fn"] == "fused_bias_gelu":
             actual = b.fused_bias_gelu_v2(*args)
+            close(actual, case["expected"], rtol=5e-6, atol=5e-6)
         elif case["fn"] == "swiglu":
             actual = b.swiglu_v0(*args)
+            close(actual, case["expected"])
         else:
             continue
-        close(actual, case["expected"])
         seen += 1
     assert seen >= 8
 

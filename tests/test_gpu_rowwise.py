@@ -143,8 +143,20 @@ def test_rowwise_golden_cases(golden):
             continue
         args = [a.to(DEV) for a in case["args"]]
         actual = ops[case["fn"]](*args, **case["kwargs"])
-        atol = 1e-3 if case["tag"] == "offset_1000" else ATOL
-        close(actual, case["expected"], rtol=RTOL, atol=atol)
+        if case["tag"] == "offset_1000":
+            # rows of 1000 + 0.1 N(0,1): fp32 LayerNorm is only accurate to
+            # ~1e-3 here (PyTorch's CPU result is off by up to 4e-3 from the
+            # float64 value), so check against float64 as the reference's own
+            # test does (tests/test_layernorm_v3.py:56-84) and loosely against
+            # the recorded CPU result.
+            x64, w64, b64 = (a.double() for a in case["args"])
+            mean = x64.mean(dim=-1, keepdim=True)
+            var = (x64 - mean).square().mean(dim=-1, keepdim=True)
+            exact = ((x64 - mean) * torch.rsqrt(var + 1e-5) * w64 + b64).float()
+            assert float((actual.cpu() - exact).abs().max()) < 2.5e-3
+            close(actual, case["expected"], rtol=RTOL, atol=1e-2)
+        else:
+            close(actual, case["expected"], rtol=RTOL, atol=ATOL)
         seen += 1
     assert seen >= 20
 
