@@ -99,4 +99,4 @@ class L2Flusher:
         self.sink = torch.empty((), dtype=torch.float32, device=dev)
 
     def __call__(self) -> None:
-        torch.sum(self.buffer, out=self.sink)
+        torch.sum(self.buffer, dim=0, out=self.sink)

@@ -99,7 +99,7 @@ class _Library:
     eagerly, so a library that lacks one fails at load time, not mid-run.
     """
 
-    def __init__(self, path: Path) -> None:
+    def __init__(self, path: Path, symbols: tuple[str, ...] | None = None) -> None:
         if not path.is_file():
             raise RuntimeError(
                 f"CUDA operator library not found at {path}. "
@@ -107,9 +107,9 @@ class _Library:
             )
         self.path = path
         self.handle = ctypes.CDLL(str(path))
-        for name, argtypes in _SIGNATURES.items():
+        for name in symbols if symbols is not None else tuple(_SIGNATURES):
             function = getattr(self.handle, name)
-            function.argtypes = argtypes
+            function.argtypes = _SIGNATURES[name]
             function.restype = _RESTYPES.get(name, ctypes.c_int)
 
     def check(self, code: int) -> None:
