@@ -13,6 +13,8 @@ COL_API const char* cuda_operator_error_string(int code) {
       return "cuTensorMapEncodeTiled rejected a GEMM operand layout";
     case col::kErrDeviceNotSupported:
       return "the tensor-core GEMM needs a compute capability 10.x (sm_100) device";
+    case col::kErrNoAllocCapacity:
+      return "cuda_operator_lab_reduction_noalloc accepts at most 268435456 (2^28) elements";
     default:
       return cudaGetErrorString(static_cast<cudaError_t>(code));
   }

@@ -18,6 +18,7 @@ namespace col {
 constexpr int kErrNoTensorMapEncoder = 10001;   // driver lacks cuTensorMapEncodeTiled
 constexpr int kErrTensorMapEncode = 10002;      // cuTensorMapEncodeTiled rejected a map
 constexpr int kErrDeviceNotSupported = 10003;   // device is not sm_100
+constexpr int kErrNoAllocCapacity = 10004;      // input larger than the allocation-free sum's scratch
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -225,3 +225,90 @@ COL_API int cuda_operator_reduction_partial_f64(const float* input, double* part
   if (n == 0) return static_cast<int>(cudaMemsetAsync(partial, 0, sizeof(double), s));
   return reduce_with_pool_scratch<true>(input, partial, n, s);
 }
+
+// ============================================================================
+// Allocation-free variant of the global sum.
+//
+// Some callers cannot let a library allocate device memory: a serving process
+// that reserved the whole device for its own allocator at start-up (any further
+// allocation fails or fragments that arena), a host framework whose policy is
+// that plugins never allocate, or a latency-critical loop where an allocator
+// call may synchronise.  For them this entry point runs the same sum kernel
+// with its scratch (one fp64 partial per CTA and a CTA counter) in a
+// fixed-size array that lives in the library image itself: no cudaMalloc,
+// cudaFree, pool or other allocating routine is ever called.
+//
+// Limits and rules, all stated to the caller in include/cuda_operator_lab.h:
+//  * the array holds kNoAllocMaxCtas partials; each CTA sums a fixed chunk of
+//    kNoAllocChunk elements, so n may not exceed kNoAllocMaxElements (2^28);
+//    larger n is rejected with kErrNoAllocCapacity before anything is launched;
+//  * every GPU that loads the library holds the array (128 KiB + 256 bytes)
+//    until the process exits;
+//  * all calls on a device share the one array: two calls whose work overlaps
+//    on the GPU (different streams, no ordering between them) race and give
+//    wrong sums; calls ordered on one stream are fine;
+//  * the array keeps the previous call's contents, so each call clears the
+//    counter (the only field that must start at zero) on its stream first;
+//  * the first call on each device looks up the array's device address
+//    (cudaGetSymbolAddress, with that device current); make that first call
+//    before any stream capture on the device.
+// ============================================================================
+
+namespace {
+
+constexpr std::uint64_t kNoAllocChunk = 16384;  // elements per CTA
+constexpr unsigned kNoAllocMaxCtas = 16384;
+constexpr std::uint64_t kNoAllocMaxElements = kNoAllocChunk * kNoAllocMaxCtas;  // 2^28
+
+// kNoAllocMaxCtas fp64 partials followed by the CTA counter (its own 256-byte
+// line).  In host code this name is only a stand-in for the symbol: the
+// kernel gets the device address found by noalloc_scratch_address().
+static __device__ __align__(256) double g_noalloc_scratch[kNoAllocMaxCtas + 32];
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device (the first call on that device); nullptr if the lookup failed.
+cudaError_t noalloc_scratch_address(double** out) {
+  constexpr int kMaxDevices = 64;
+  static double* addrs[kMaxDevices] = {};
+  static cudaError_t errors[kMaxDevices] = {};
+  static std::once_flag flags[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::call_once(flags[dev], [dev]() {
+    void* p = nullptr;
+    errors[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    addrs[dev] = errors[dev] == cudaSuccess ? static_cast<double*>(p) : nullptr;
+  });
+  *out = addrs[dev];
+  return errors[dev];
+}
+
+}  // namespace
+
+COL_API int cuda_operator_lab_reduction_noalloc(const float* input, float* output, uint64_t n,
+                                                void* stream) {
+  if (output == nullptr || (input == nullptr && n != 0)) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  if (n > kNoAllocMaxElements) return col::kErrNoAllocCapacity;
+  const cudaStream_t s = col::as_stream(stream);
+  if (n == 0) return static_cast<int>(cudaMemsetAsync(output, 0, sizeof(float), s));
+  double* scratch = nullptr;
+  const cudaError_t e = noalloc_scratch_address(&scratch);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  double* partials = scratch;
+  unsigned* counter = reinterpret_cast<unsigned*>(scratch + kNoAllocMaxCtas);
+  const cudaError_t ms = cudaMemsetAsync(counter, 0, sizeof(unsigned), s);
+  if (ms != cudaSuccess) return static_cast<int>(ms);
+  const unsigned ctas = static_cast<unsigned>((n + kNoAllocChunk - 1) / kNoAllocChunk);
+  if (col::aligned16(input)) {
+    sum_kernel<true, false><<<ctas, kThreads, 0, s>>>(input, n, kNoAllocChunk, partials, counter,
+                                                      output);
+  } else {
+    sum_kernel<false, false><<<ctas, kThreads, 0, s>>>(input, n, kNoAllocChunk, partials, counter,
+                                                       output);
+  }
+  return static_cast<int>(cudaGetLastError());
+}

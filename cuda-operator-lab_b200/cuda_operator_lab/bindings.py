@@ -71,6 +71,7 @@ _SIGNATURES["cuda_operator_reduction_partial_f64"] = [_P, _P, _U64, _P]
 _SIGNATURES["cuda_operator_lab_device_info"] = [_P, _P, _P]
 _SIGNATURES["cuda_operator_lab_build_tag"] = []
 _SIGNATURES["cuda_operator_lab_gemm_status"] = [_P, _I32]
+_SIGNATURES["cuda_operator_lab_reduction_noalloc"] = [_P, _P, _U64, _P]
 
 _RESTYPES = {
     "cuda_operator_error_string": ctypes.c_char_p,

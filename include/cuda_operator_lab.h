@@ -165,6 +165,20 @@ int cuda_operator_gemm_bias_gelu_bf16(const void* input_bf16, const void* weight
  * the global sum. */
 int cuda_operator_reduction_partial_f64(const float* input, double* partial, uint64_t n, void* stream);
 
+/* Global fp32 sum that allocates no device memory.  No counterpart in the
+ * reference: it is for callers that cannot let a library allocate (a server
+ * that reserved the whole device for its own allocator at start-up, a host
+ * whose plugins must not allocate, a loop where an allocator call could
+ * synchronise).  Same result contract as cuda_operator_reduction_v*, computed
+ * by the same kernel, with its scratch in a fixed 128 KiB array inside the
+ * library image (held by every GPU that loads the library until exit).
+ * Accepts n <= 268435456 (2^28); larger n returns 10004 before any launch.
+ * All calls on a device share that array: calls whose GPU work overlaps
+ * (unordered streams) race; calls ordered on one stream are safe.  Each call
+ * clears the array's counter on its stream first.  The first call on a device
+ * looks up the array's device address; make it before any stream capture. */
+int cuda_operator_lab_reduction_noalloc(const float* input, float* output, uint64_t n, void* stream);
+
 /* Number of SMs of the current device and the library's build tag; lets a
  * caller check which library it loaded.  Host-only, enqueues nothing. */
 int cuda_operator_lab_device_info(int* sm_count, int* cc_major, int* cc_minor);
