@@ -532,7 +532,7 @@ KERNEL_CASES = ("gemm_swiglu_bf16", "gemm_bias_gelu_bf16", "rmsnorm_bf16", "redu
                 "rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "bias_gelu_fp32", "swiglu_fp32")
 
 
-def run_kernel_case(spec: str, reps: int) -> None:
+def run_kernel_case(spec: str, reps: int, timed: bool = False) -> None:
     """Launch one op `reps` times at a given size and exit: the command that
     profilers (ncu) wrap.  spec = NAME[:d0,d1,...], e.g. gemm_swiglu_bf16:2048,4096,14336."""
     from cuda_operator_lab import bindings as b
@@ -576,12 +576,30 @@ def run_kernel_case(spec: str, reps: int) -> None:
               "layernorm_fp32": lambda: b.layernorm_v5_into(x, w, bias, y),
               "bias_gelu_fp32": lambda: b.fused_bias_gelu_v2_into(x, bias, y),
               "swiglu_fp32": lambda: b.swiglu_v2_into(x, u, y)}[name]
-    for _ in range(reps):
-        fn()
-    torch.cuda.synchronize()
+    if not timed:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+        return
+    from cuda_operator_lab.benchmarking import L2Flusher, measure_batch_us
+
+    warm = measure_batch_us(fn, warmup=3, repeats=max(reps, 10))
+    cold = event_median_us(fn, max(reps, 10), L2Flusher(dev))
+    print(json.dumps({"kernel_case": spec, "us_warm_back_to_back": round(warm, 3),
+                      "us_cold_single": round(cold, 3)}), file=sys.stderr)
+
+
+def _json_stdout():
+    """Keep stdout for the one JSON line: anything else written to fd 1 (NCCL's
+    version banner, library prints) is sent to stderr."""
+    out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
+    return out
 
 
 def main() -> None:
+    json_out = _json_stdout()
     parser = argparse.ArgumentParser(description=__doc__,
                                      formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
@@ -594,9 +612,11 @@ def main() -> None:
     parser.add_argument("--kernel-case", default=None,
                         help="run one op only (for profilers): NAME[:dims], see KERNEL_CASES")
     parser.add_argument("--reps", type=int, default=3)
+    parser.add_argument("--time", action="store_true",
+                        help="with --kernel-case: print warm and cold CUDA-event times")
     args = parser.parse_args()
     if args.kernel_case:
-        run_kernel_case(args.kernel_case, args.reps)
+        run_kernel_case(args.kernel_case, args.reps, args.time)
         return
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -604,7 +624,7 @@ def main() -> None:
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) != 0:
             return  # rank 0 alone times the CPU path
-        print(json.dumps(run_reference(args)))
+        print(json.dumps(run_reference(args)), file=json_out, flush=True)
         return
 
     d = Dist()
@@ -615,7 +635,7 @@ def main() -> None:
     finally:
         d.close()
     if result is not None:
-        print(json.dumps(result))
+        print(json.dumps(result), file=json_out, flush=True)
 
 
 if __name__ == "__main__":

@@ -11,6 +11,7 @@
 
 #include "gemm_simt.cuh"
 #include "gemm_sm100.cuh"
+#include "gemm_sm100_2sm.cuh"
 
 namespace {
 
@@ -78,11 +79,92 @@ int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
   }
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int grid = tiles < sm_count ? tiles : sm_count;
-  kernel<<<grid, 256, Cfg::kSmemBytes, s>>>(p);
+  kernel<<<grid, col::sm100::kCtaThreads, Cfg::kSmemBytes, s>>>(p);
   return static_cast<int>(cudaGetLastError());
 }
 
+// CTA pairs (2-SM kernel) that can be resident at once on the current device
+// (cudaOccupancyMaxActiveClusters for one instantiation; every BNH variant
+// uses over half of the shared memory, so all fit one CTA per SM and share
+// the answer).  Queried once per device; 0 if clusters are unavailable.
+template <int EPI, typename TOut>
+int max_pair_clusters(int dev) {
+  using Cfg = col::sm100::TileCfg2<128>;
+  static int cached[64] = {};
+  static std::once_flag flags[64];
+  std::call_once(flags[dev & 63], [dev]() {
+    auto kernel = col::sm100::gemm_bf16_tc2_kernel<128, EPI, TOut>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(col::sm100::kCtaThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters <= 0) {
+      cudaGetLastError();  // clear the error; fall back to the 1-CTA kernel
+      clusters = 0;
+    }
+    cached[dev & 63] = clusters;
+  });
+  return cached[dev & 63];
+}
+
+template <int BNH, int EPI, typename TOut>
+int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
+  using Cfg = col::sm100::TileCfg2<BNH>;
+  auto kernel = col::sm100::gemm_bf16_tc2_kernel<BNH, EPI, TOut>;
+  const int tiles = p.num_m_blocks * p.num_n_blocks;
+  const int grid = 2 * (tiles < clusters ? tiles : clusters);
+  kernel<<<grid, col::sm100::kCtaThreads, Cfg::kSmemBytes, s>>>(p);
+  (void)dev;
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int BNH, int EPI, typename TOut>
+int set_smem_attr_2sm(int dev) {
+  using Cfg = col::sm100::TileCfg2<BNH>;
+  static std::atomic<std::uint64_t> attr_set{0};
+  const std::uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_set.load(std::memory_order_acquire) & bit)) {
+    const cudaError_t e = cudaFuncSetAttribute(col::sm100::gemm_bf16_tc2_kernel<BNH, EPI, TOut>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(Cfg::kSmemBytes));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_set.fetch_or(bit, std::memory_order_release);
+  }
+  return 0;
+}
+
 enum class BMode { kSwiGLU, kGelu };
+
+// Tile width: the B box height BNH (MMA N = 2*BNH; output columns per tile =
+// BNH for SwiGLU, 2*BNH for GELU).  The persistent grid processes tiles in
+// waves of sm_count; a tile's main loop costs ~2*BNH MMA columns per k-block,
+// so the cost of a choice is waves * 2*BNH.  Ties go to the wider tile (fewer
+// epilogues, better MMA efficiency).  Example: M=512, N=4096 SwiGLU gives 128
+// tiles at BNH=128 (one 86 %-full wave) but exactly 148 at BNH=112.
+int choose_bnh(int mblocks, std::uint64_t n, bool swiglu, int sm_count) {
+  constexpr int kCandidates[] = {128, 112, 96, 64};
+  int best = 128;
+  std::uint64_t best_cost = ~0ull;
+  for (int bnh : kCandidates) {
+    const std::uint64_t cols = swiglu ? bnh : 2 * bnh;
+    const std::uint64_t tiles = static_cast<std::uint64_t>(mblocks) * ((n + cols - 1) / cols);
+    const std::uint64_t waves = (tiles + sm_count - 1) / sm_count;
+    const std::uint64_t cost = waves * 2 * bnh;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bnh;
+    }
+  }
+  return best;
+}
 
 // bf16 tensor-core path.  For kSwiGLU, w0/w1 are the gate/up matrices [n, k];
 // for kGelu, w0 is W [n, k] (w1 ignored).  Returns -1 when TMA cannot address
@@ -101,12 +183,18 @@ int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, cons
   if (!status) return static_cast<int>(cudaErrorInvalidDevice);
 
   const int mblocks = static_cast<int>((m + 127) / 128);
-  // Output columns per tile: BNH for SwiGLU, 2*BNH for bias+GELU.
-  const auto tiles_for = [&](int bnh) {
-    const std::uint64_t cols = mode == BMode::kSwiGLU ? bnh : 2 * bnh;
-    return static_cast<std::uint64_t>(mblocks) * ((n + cols - 1) / cols);
-  };
-  const int bnh = tiles_for(128) >= static_cast<std::uint64_t>(info.sm_count) / 2 ? 128 : 64;
+  // CTA-pair kernel when there are at least two 128-row blocks: half of each
+  // weight tile per SM.  Its BNH choice uses pair blocks and pair slots.
+  const bool pair = mblocks >= 2;
+  int pair_slots = 0;
+  if (pair) {
+    if (int rc = set_smem_attr_2sm<128, EPI, TOut>(dev)) return rc;
+    pair_slots = max_pair_clusters<EPI, TOut>(dev);
+  }
+  const bool use_pair = pair && pair_slots > 0;
+  const int mblocks_sched = use_pair ? (mblocks + 1) / 2 : mblocks;
+  const int bnh = choose_bnh(mblocks_sched, n, mode == BMode::kSwiGLU,
+                             use_pair ? pair_slots : info.sm_count);
 
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
@@ -121,7 +209,7 @@ int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, cons
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
-  p.num_m_blocks = mblocks;
+  p.num_m_blocks = mblocks_sched;
   p.num_k_blocks = static_cast<int>((k + col::sm100::kBlockK - 1) / col::sm100::kBlockK);
   if (mode == BMode::kSwiGLU) {
     p.num_n_blocks = static_cast<int>((n + bnh - 1) / bnh);
@@ -132,10 +220,33 @@ int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, cons
     p.b_row_stride = 2 * bnh;
     p.b1_row_offset = bnh;
   }
+  // Few M-blocks per weight tile: the weights stream from DRAM with little L2
+  // reuse, so warm L2 ahead of the ring.  Many M-blocks: the raster already
+  // keeps each weight tile L2-resident across its M-group.
+  p.prefetch_b = mblocks <= 8 ? 1 : 0;
   p.out_ld = static_cast<int>(n);
   p.out_vec_ok = col::aligned16(out) && ((n * sizeof(TOut)) % 16 == 0);
-  if (bnh == 128) return launch_tc<128, EPI, TOut>(p, s, dev, info.sm_count);
-  return launch_tc<64, EPI, TOut>(p, s, dev, info.sm_count);
+  if (use_pair) {
+    int rc = 0;
+    switch (bnh) {
+      case 128: return launch_tc2<128, EPI, TOut>(p, s, dev, pair_slots);
+      case 112:
+        if ((rc = set_smem_attr_2sm<112, EPI, TOut>(dev))) return rc;
+        return launch_tc2<112, EPI, TOut>(p, s, dev, pair_slots);
+      case 96:
+        if ((rc = set_smem_attr_2sm<96, EPI, TOut>(dev))) return rc;
+        return launch_tc2<96, EPI, TOut>(p, s, dev, pair_slots);
+      default:
+        if ((rc = set_smem_attr_2sm<64, EPI, TOut>(dev))) return rc;
+        return launch_tc2<64, EPI, TOut>(p, s, dev, pair_slots);
+    }
+  }
+  switch (bnh) {
+    case 128: return launch_tc<128, EPI, TOut>(p, s, dev, info.sm_count);
+    case 112: return launch_tc<112, EPI, TOut>(p, s, dev, info.sm_count);
+    case 96: return launch_tc<96, EPI, TOut>(p, s, dev, info.sm_count);
+    default: return launch_tc<64, EPI, TOut>(p, s, dev, info.sm_count);
+  }
 }
 
 template <typename TIn, int EPI, typename TOut>

@@ -1,7 +1,7 @@
 // Blackwell (sm_100a) tensor-core GEMM with fused SwiGLU / bias+GELU
 // epilogues: D[M, N'] = X[M, K] . B[N', K]^T, bf16 operands, fp32 accumulate.
 //
-// Persistent, warp-specialised CTA (256 threads, one CTA per SM):
+// Persistent, warp-specialised CTA (384 threads, one CTA per SM):
 //   warp 0      TMA producer: one thread streams 128x64 X tiles and two
 //               BNHx64 B boxes per k-block into a STAGES-deep smem ring
 //               (128-byte swizzle, completion counted on an mbarrier);
@@ -9,7 +9,8 @@
 //               K=16) from the smem descriptors into a TMEM accumulator and
 //               releases ring slots with tcgen05.commit;
 //   warp 2      allocates/frees the TMEM columns;
-//   warps 4..7  epilogue: tcgen05.ld the accumulator (one row per thread),
+//   warps 4..11 epilogue: tcgen05.ld the accumulator (one row per thread,
+//               two warps per TMEM lane quarter splitting the columns),
 //               apply silu(g)*u or gelu(acc+bias) in registers, store once.
 // Two TMEM accumulators alternate between tiles, so the epilogue of tile i
 // overlaps the main loop of tile i+1.
@@ -44,6 +45,10 @@ enum Epilogue : int {
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;  // bf16 elements per k-block: one 128-byte swizzle row
 constexpr int kGroupM = 16;  // m-blocks per rasterisation group (L2 reuse of B)
+constexpr int kPrefetchDepth = 8;  // k-blocks between an L2 prefetch and its load
+constexpr int kEpiWarps = 8;       // warps 4..11: two per TMEM lane quarter
+constexpr int kEpiGroups = kEpiWarps / 4;
+constexpr int kCtaThreads = 128 + 32 * kEpiWarps;  // producer, MMA, TMEM, idle + epilogue
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 // Status bits written on a bounded-wait timeout.
@@ -69,19 +74,35 @@ struct __align__(64) GemmParams {
   int b1_row_offset;  // box-1 row relative to box 0
   int out_ld;         // output row stride in elements
   int out_vec_ok;     // 16-byte vector stores allowed
+  int prefetch_b;     // issue L2 prefetches for B boxes ahead of the ring
 };
 
+constexpr uint32_t kSmemLimit = 232448;  // max dynamic shared memory per CTA on sm_100
+
+__host__ __device__ constexpr uint32_t pow2_at_least(uint32_t v) {
+  uint32_t p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+// BNH = rows of each B box (gate/up half, or half of the GELU tile); the MMA
+// is M=128 x N=2*BNH.  BNH must keep the box a whole number of 1024-byte
+// swizzle atoms (BNH % 8 == 0) and 2*BNH a multiple of 16 in [16, 256].
 template <int BNH>
 struct TileCfg {
+  static_assert(BNH % 16 == 0 && BNH >= 32 && BNH <= 128, "unsupported B box height");
   static constexpr int kMmaN = 2 * BNH;
   static constexpr uint32_t kABytes = kBlockM * kBlockK * 2;
   static constexpr uint32_t kBBytes = kMmaN * kBlockK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = BNH == 128 ? 4 : 6;
-  static constexpr uint32_t kAccCols = kMmaN;
-  static constexpr uint32_t kTmemCols = 2 * kAccCols;
   static constexpr uint32_t kBarrierBytes = 256;
+  static constexpr int kStagesFit = static_cast<int>((kSmemLimit - 1024 - kBarrierBytes) / kStageBytes);
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr uint32_t kAccStride = pow2_at_least(kMmaN);  // TMEM columns per accumulator
+  static constexpr uint32_t kTmemCols = 2 * kAccStride;
   static constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+  static_assert(kTmemCols <= 512, "two accumulators must fit in TMEM");
+  static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -123,14 +144,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Bounded wait: true when the phase of `parity` completed; false after the
 // time limit or when another role raised the abort flag.
+// The clock is first read only after 64 failed polls, so short waits (the
+// common case) never pay for a %globaltimer read.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  uint64_t t0 = 0;
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0u) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        return false;
+      }
     }
   }
 }
@@ -151,6 +178,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
       : "memory");
+}
+
+// Warm L2 with a box that a later stage will load (no shared memory, no
+// completion tracking; a hint the hardware may drop).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
@@ -226,6 +262,47 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Two 16-column loads (e.g. the gate and the up columns of one output chunk)
+// completed by one wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, uint32_t (&a)[16],
+                                            uint32_t (&b)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%32];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%33];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]),
+        "=r"(a[7]), "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]),
+        "=r"(a[14]), "=r"(a[15]), "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]),
+        "=r"(b[5]), "=r"(b[6]), "=r"(b[7]), "=r"(b[8]), "=r"(b[9]), "=r"(b[10]), "=r"(b[11]),
+        "=r"(b[12]), "=r"(b[13]), "=r"(b[14]), "=r"(b[15])
+      : "r"(ta), "r"(tb)
+      : "memory");
+}
+
+template <int W>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[W]) {
+  if constexpr (W == 32) {
+    tmem_ld32(taddr, r);
+  } else {
+    static_assert(W == 16, "chunk width");
+    tmem_ld16(taddr, r);
+  }
+}
+
 // ------------------------------------------------------------ tile schedule
 
 __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& mb, int& nb) {
@@ -240,22 +317,22 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& 
 
 // ------------------------------------------------------------ epilogue store
 
-template <typename TOut>
-__device__ __forceinline__ void store_chunk32(const GemmParams& p, int row, int col0,
-                                              const float (&o)[32]) {
+template <typename TOut, int W>
+__device__ __forceinline__ void store_chunk(const GemmParams& p, int row, int col0,
+                                            const float (&o)[W]) {
   if (row >= p.m) return;
   TOut* dst = static_cast<TOut*>(p.out) + static_cast<std::size_t>(row) * p.out_ld + col0;
-  if (p.out_vec_ok && col0 + 32 <= p.n) {
+  if (p.out_vec_ok && col0 + W <= p.n) {
     if constexpr (sizeof(TOut) == 4) {
       float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < W / 4; ++j) {
         __stcs(d4 + j, make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]));
       }
     } else {
       uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < W / 8; ++j) {
         uint4 v;
         v.x = pack_bf16x2(o[8 * j + 0], o[8 * j + 1]);
         v.y = pack_bf16x2(o[8 * j + 2], o[8 * j + 3]);
@@ -266,7 +343,7 @@ __device__ __forceinline__ void store_chunk32(const GemmParams& p, int row, int 
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < W; ++j) {
       if (col0 + j < p.n) {
         if constexpr (sizeof(TOut) == 4) {
           dst[j] = o[j];
@@ -278,14 +355,64 @@ __device__ __forceinline__ void store_chunk32(const GemmParams& p, int row, int 
   }
 }
 
+// ------------------------------------------------------------ epilogue
+
+// One accumulator tile, this thread's TMEM lane (one output row): 16-column
+// chunks dealt round-robin to the kEpiGroups warps that share the lane
+// quarter.  SwiGLU: gate at accumulator column c, up at BNH + c, output
+// column nb*BNH + c.  GELU: accumulator column c is output nb*2*BNH + c.
+template <int BNH, int EPI, typename TOut>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, int row, int nb, uint32_t t_row,
+                                              int group) {
+  if constexpr (EPI == kEpiSwiGLU || EPI == kEpiSwiGLURoundBf16) {
+    const int col_base = nb * BNH;
+#pragma unroll 1
+    for (int c = group * 16; c < BNH; c += 16 * kEpiGroups) {
+      uint32_t g[16], u[16];
+      tmem_ld16x2(t_row + c, t_row + BNH + c, g, u);
+      float o[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float gv = __uint_as_float(g[j]);
+        float uv = __uint_as_float(u[j]);
+        if constexpr (EPI == kEpiSwiGLURoundBf16) {
+          gv = bf16_round(gv);
+          uv = bf16_round(uv);
+        }
+        o[j] = silu_fast(gv) * uv;
+      }
+      store_chunk<TOut, 16>(p, row, col_base + c, o);
+    }
+  } else {
+    const int col_base = nb * 2 * BNH;
+#pragma unroll 1
+    for (int c = group * 16; c < 2 * BNH; c += 16 * kEpiGroups) {
+      uint32_t a[16];
+      tmem_ld16(t_row + c, a);
+      float o[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int colj = col_base + c + j;
+        const float bv = colj < p.n ? __ldg(p.bias + colj) : 0.0f;
+        const float z = __uint_as_float(a[j]) + bv;
+        if constexpr (EPI == kEpiBiasGeluErf) {
+          o[j] = gelu_erf_f(z);
+        } else {
+          o[j] = gelu_tanh_f(z);
+        }
+      }
+      store_chunk<TOut, 16>(p, row, col_base + c, o);
+    }
+  }
+}
+
 // ------------------------------------------------------------ the kernel
 
 template <int BNH, int EPI, typename TOut>
-__global__ void __launch_bounds__(256, 1) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
   using Cfg = TileCfg<BNH>;
   constexpr int kStages = Cfg::kStages;
   constexpr uint32_t kIdesc = idesc_bf16_f32(kBlockM, Cfg::kMmaN);
-  constexpr bool kSwiGLU = (EPI == kEpiSwiGLU || EPI == kEpiSwiGLURoundBf16);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -310,7 +437,7 @@ __global__ void __launch_bounds__(256, 1) gemm_bf16_tc_kernel(const __grid_const
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(tfull_bar + a), 1);
-      mbar_init(smem_u32(tempty_bar + a), 4);
+      mbar_init(smem_u32(tempty_bar + a), kEpiWarps);
     }
     mbar_init(smem_u32(drain_bar), 1);
     *abort_flag = 0;
@@ -359,6 +486,14 @@ __global__ void __launch_bounds__(256, 1) gemm_bf16_tc_kernel(const __grid_const
           tma_load_2d(sa, &p.map_a, fb, kx, a_row);
           tma_load_2d(sb, &p.map_b0, fb, kx, b0_row);
           tma_load_2d(sb + BNH * 128, &p.map_b1, fb, kx, b1_row);
+          // Weight boxes kPrefetchDepth k-blocks ahead go to L2 now, so when
+          // the ring reaches them the TMA reads hit L2 instead of waiting on
+          // DRAM (matters when few M-blocks share each weight tile).
+          if (p.prefetch_b && kb + kPrefetchDepth < p.num_k_blocks) {
+            const int px = kx + kPrefetchDepth * kBlockK;
+            tma_prefetch_l2_2d(&p.map_b0, px, b0_row);
+            tma_prefetch_l2_2d(&p.map_b1, px, b1_row);
+          }
           issued_mask |= 1u << stage;
           issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == kStages) {
@@ -394,7 +529,7 @@ __global__ void __launch_bounds__(256, 1) gemm_bf16_tc_kernel(const __grid_const
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccCols;
+        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
         for (int kb = 0; kb < p.num_k_blocks; ++kb) {
           if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
             fail(kStatusMma);
@@ -426,8 +561,10 @@ __global__ void __launch_bounds__(256, 1) gemm_bf16_tc_kernel(const __grid_const
       }
     }
   } else if (warp >= 4) {
-    // ---------------- epilogue: warp (4 + q) owns TMEM lanes [32q, 32q + 32)
-    const int q = warp - 4;
+    // ---------------- epilogue: warp w owns TMEM lanes [32q, 32q + 32) with
+    // q = w % 4; the kEpiGroups warps of a quarter split its columns.
+    const int q = warp & 3;
+    const int group = (warp - 4) >> 2;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -443,48 +580,8 @@ __global__ void __launch_bounds__(256, 1) gemm_bf16_tc_kernel(const __grid_const
       }
       tc_fence_after();
       const int row = mb * kBlockM + q * 32 + lane;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccCols;
-      if constexpr (kSwiGLU) {
-        const int col_base = nb * BNH;
-#pragma unroll 1
-        for (int c = 0; c < BNH; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld32(t_row + c, g);
-          tmem_ld32(t_row + BNH + c, u);
-          float o[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float gv = __uint_as_float(g[j]);
-            float uv = __uint_as_float(u[j]);
-            if constexpr (EPI == kEpiSwiGLURoundBf16) {
-              gv = bf16_round(gv);
-              uv = bf16_round(uv);
-            }
-            o[j] = silu_f(gv) * uv;
-          }
-          store_chunk32<TOut>(p, row, col_base + c, o);
-        }
-      } else {
-        const int col_base = nb * 2 * BNH;
-#pragma unroll 1
-        for (int c = 0; c < 2 * BNH; c += 32) {
-          uint32_t a[32];
-          tmem_ld32(t_row + c, a);
-          float o[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int colj = col_base + c + j;
-            const float bv = colj < p.n ? __ldg(p.bias + colj) : 0.0f;
-            const float z = __uint_as_float(a[j]) + bv;
-            if constexpr (EPI == kEpiBiasGeluErf) {
-              o[j] = gelu_erf_f(z);
-            } else {
-              o[j] = gelu_tanh_f(z);
-            }
-          }
-          store_chunk32<TOut>(p, row, col_base + c, o);
-        }
-      }
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccStride;
+      epilogue_tile<BNH, EPI, TOut>(p, row, nb, t_row, group);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(tempty_bar + acc));

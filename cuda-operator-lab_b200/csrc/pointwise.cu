@@ -79,33 +79,37 @@ int swiglu_launch(const float* g, const float* u, float* o, std::uint64_t n, cud
 
 // ---------------------------------------------------------------- bias + GELU
 
-// Each CTA walks whole rows, so the bias column of a vector is its position
-// in the row (no per-element modulo); the bias row stays in L1.
+// 2-D decomposition: blockIdx.x picks 256 float4 columns, blockIdx.y strides
+// over rows.  Each thread loads its bias vector once and reuses it for every
+// row it visits (no per-element modulo, no repeated bias loads), with kUnroll
+// rows in flight.
 __global__ void __launch_bounds__(kThreads)
 bias_gelu_vec_kernel(const float4* __restrict__ x, const float4* __restrict__ b,
-                     float4* __restrict__ o, std::uint64_t rows, std::uint32_t vcols) {
-  const std::uint64_t total = rows * vcols;
-  const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
-  std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  for (; i + (kUnroll - 1) * stride < total; i += kUnroll * stride) {
+                     float4* __restrict__ o, std::uint32_t rows, std::uint32_t vcols) {
+  const std::uint32_t c = blockIdx.x * kThreads + threadIdx.x;
+  if (c >= vcols) return;
+  const float4 bv = __ldg(b + c);
+  const std::uint32_t rstride = gridDim.y;
+  std::uint32_t r = blockIdx.y;
+  for (; r + (kUnroll - 1) * rstride < rows; r += kUnroll * rstride) {
     float4 xv[kUnroll];
 #pragma unroll
-    for (int j = 0; j < kUnroll; ++j) xv[j] = col::ld_stream_f4(x + i + j * stride);
+    for (int j = 0; j < kUnroll; ++j) {
+      xv[j] = col::ld_stream_f4(x + static_cast<std::uint64_t>(r + j * rstride) * vcols + c);
+    }
 #pragma unroll
     for (int j = 0; j < kUnroll; ++j) {
-      const std::uint64_t idx = i + j * stride;
-      const float4 bv = __ldg(b + static_cast<std::uint32_t>(idx % vcols));
-      float4 r;
-      r.x = col::gelu_erf_f(xv[j].x + bv.x);
-      r.y = col::gelu_erf_f(xv[j].y + bv.y);
-      r.z = col::gelu_erf_f(xv[j].z + bv.z);
-      r.w = col::gelu_erf_f(xv[j].w + bv.w);
-      col::st_stream_f4(o + idx, r);
+      float4 v;
+      v.x = col::gelu_erf_f(xv[j].x + bv.x);
+      v.y = col::gelu_erf_f(xv[j].y + bv.y);
+      v.z = col::gelu_erf_f(xv[j].z + bv.z);
+      v.w = col::gelu_erf_f(xv[j].w + bv.w);
+      col::st_stream_f4(o + static_cast<std::uint64_t>(r + j * rstride) * vcols + c, v);
     }
   }
-  for (; i < total; i += stride) {
+  for (; r < rows; r += rstride) {
+    const std::uint64_t i = static_cast<std::uint64_t>(r) * vcols + c;
     const float4 xv = col::ld_stream_f4(x + i);
-    const float4 bv = __ldg(b + static_cast<std::uint32_t>(i % vcols));
     col::st_stream_f4(o + i, make_float4(col::gelu_erf_f(xv.x + bv.x), col::gelu_erf_f(xv.y + bv.y),
                                          col::gelu_erf_f(xv.z + bv.z), col::gelu_erf_f(xv.w + bv.w)));
   }
@@ -131,11 +135,20 @@ int bias_gelu(const float* x, const float* b, float* o, std::uint64_t rows, std:
   }
   const cudaStream_t s = col::as_stream(stream);
   const std::uint32_t c = static_cast<std::uint32_t>(cols);
-  if ((c % 4) == 0 && col::aligned16(x) && col::aligned16(b) && col::aligned16(o)) {
+  if ((c % 4) == 0 && col::aligned16(x) && col::aligned16(b) && col::aligned16(o) &&
+      rows <= 0xffffffffull) {
     const std::uint32_t vcols = c / 4;
-    bias_gelu_vec_kernel<<<grid_for(rows * vcols, kUnroll), kThreads, 0, s>>>(
+    const unsigned gx = (vcols + kThreads - 1) / kThreads;
+    // rows per column-block: enough CTAs for ~8 per SM, each visiting >= kUnroll rows
+    const std::uint64_t target = static_cast<std::uint64_t>(col::device_info().sm_count) * 8;
+    std::uint64_t gy = (target + gx - 1) / gx;
+    const std::uint64_t max_gy = (rows + kUnroll - 1) / kUnroll;
+    if (gy > max_gy) gy = max_gy;
+    if (gy > 65535) gy = 65535;
+    if (gy == 0) gy = 1;
+    bias_gelu_vec_kernel<<<dim3(gx, static_cast<unsigned>(gy)), kThreads, 0, s>>>(
         reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(b),
-        reinterpret_cast<float4*>(o), rows, vcols);
+        reinterpret_cast<float4*>(o), static_cast<std::uint32_t>(rows), vcols);
   } else {
     bias_gelu_scalar_kernel<<<grid_for(rows * c, 1), kThreads, 0, s>>>(x, b, o, rows, c);
   }

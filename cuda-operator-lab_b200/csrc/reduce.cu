@@ -16,7 +16,7 @@
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kCtasPerSm = 8;                   // 256-thread CTAs resident per SM
+constexpr int kCtasPerSm = 8;                   // fallback: 256-thread CTAs per SM
 constexpr std::uint64_t kChunkQuantum = 1024;   // elements: one float4 per thread
 constexpr std::uint64_t kMinChunk = 4096;
 
@@ -25,11 +25,37 @@ struct Plan {
   unsigned ctas;
 };
 
-// One wave: at most sm_count * 8 CTAs, every chunk the same size (a multiple
-// of 1024 elements, so chunk starts keep 16-byte alignment), so all CTAs are
-// resident at once and finish together.
+template <bool VEC, bool OUT_F64>
+__global__ void sum_kernel(const float* __restrict__ x, std::uint64_t n, std::uint64_t per_cta,
+                           double* __restrict__ partials, unsigned* __restrict__ counter, void* out);
+
+// CTAs of sum_kernel resident per SM on the current device (occupancy API,
+// queried once per device); the one-wave grid is sm_count times this.
+int resident_ctas_per_sm() {
+  constexpr int kMaxDevices = 64;
+  static int cached[kMaxDevices] = {};
+  static std::once_flag flags[kMaxDevices];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) return kCtasPerSm;
+  std::call_once(flags[dev], [dev]() {
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, sum_kernel<true, false>, kThreads,
+                                                      0) != cudaSuccess ||
+        blocks <= 0) {
+      blocks = kCtasPerSm;
+    }
+    cached[dev] = blocks;
+  });
+  return cached[dev];
+}
+
+// One wave: at most sm_count x (CTAs resident per SM), every chunk the same
+// size (a multiple of 1024 elements, so chunk starts keep 16-byte alignment),
+// so all CTAs are resident at once and finish together.
 Plan plan_for(std::uint64_t n) {
-  const std::uint64_t target = static_cast<std::uint64_t>(col::device_info().sm_count) * kCtasPerSm;
+  const std::uint64_t target =
+      static_cast<std::uint64_t>(col::device_info().sm_count) * resident_ctas_per_sm();
   std::uint64_t per = (n + target - 1) / target;
   per = (per + kChunkQuantum - 1) / kChunkQuantum * kChunkQuantum;
   if (per < kMinChunk) per = kMinChunk;
