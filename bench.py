@@ -357,8 +357,11 @@ def op_table(d: Dist, pk: dict) -> dict:
     xf = randn(512, 4096)
     wf = randn(4096, 4096, scale=4096 ** -0.5)
     of = torch.empty(512, 4096, device=dev)
-    tc_op("gemm_bias_gelu_fp32_512x4096x4096_v6_cudacores", lambda: b.gemm_bias_gelu_v6_into(
-        xf, wf, bg, of), 2 * 512 * 4096 * 4096, reps=5)
+    tc_op("gemm_bias_gelu_fp32_512x4096x4096_v0", lambda: b.gemm_bias_gelu_v0_into(
+        xf, wf, bg, of), 2 * 512 * 4096 * 4096, reps=20)
+    wf2 = randn(8192, 4096, scale=4096 ** -0.5)
+    tc_op("gemm_swiglu_fp32_512x4096x4096_v3", lambda: b.gemm_swiglu_v3_into(
+        xf, wf2, ws32, o32), fl, reps=20)
     return ops
 
 
@@ -529,7 +532,8 @@ def run_reference(args) -> dict:
 
 
 KERNEL_CASES = ("gemm_swiglu_bf16", "gemm_bias_gelu_bf16", "rmsnorm_bf16", "reduction",
-                "rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "bias_gelu_fp32", "swiglu_fp32")
+                "rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "bias_gelu_fp32", "swiglu_fp32",
+                "gemm_bias_gelu_fp32", "gemm_swiglu_fp32")
 
 
 def run_kernel_case(spec: str, reps: int, timed: bool = False) -> None:
@@ -555,6 +559,16 @@ def run_kernel_case(spec: str, reps: int, timed: bool = False) -> None:
         x, w, bias = rn(m, k).bfloat16(), (rn(n, k) * k ** -0.5).bfloat16(), rn(n) * 0.1
         out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
         fn = lambda: b.gemm_bias_gelu_bf16_into(x, w, bias, out)  # noqa: E731
+    elif name == "gemm_bias_gelu_fp32":
+        m, k, n = d or (512, 4096, 4096)
+        x, w, bias = rn(m, k), rn(n, k) * k ** -0.5, rn(n) * 0.1
+        out = torch.empty(m, n, device=dev)
+        fn = lambda: b.gemm_bias_gelu_v0_into(x, w, bias, out)  # noqa: E731
+    elif name == "gemm_swiglu_fp32":
+        m, k, n = d or (512, 4096, 4096)
+        x, w = rn(m, k), rn(2 * n, k) * k ** -0.5
+        ws, out = torch.empty(m, 2 * n, device=dev), torch.empty(m, n, device=dev)
+        fn = lambda: b.gemm_swiglu_v3_into(x, w, ws, out)  # noqa: E731
     elif name == "rmsnorm_bf16":
         r, c = d or (M, K)
         x, w = rn(r, c).bfloat16(), (torch.rand(c, device=dev, generator=g) + 0.5).bfloat16()

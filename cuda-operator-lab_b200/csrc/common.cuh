@@ -35,6 +35,10 @@ struct DeviceInfo {
   int max_smem_optin = 0;
 };
 
+// Library-owned stream-ordered memory pool of the current device (freed
+// blocks stay mapped), shared by the operators that need scratch.
+cudaError_t library_pool(cudaMemPool_t* pool);
+
 inline const DeviceInfo& device_info(int* device_out = nullptr) {
   constexpr int kMaxDevices = 64;
   static DeviceInfo infos[kMaxDevices];

@@ -65,10 +65,10 @@ int encode_bf16_rows(CUtensorMap* map, const void* base, std::uint64_t rows, std
   return r == CUDA_SUCCESS ? 0 : col::kErrTensorMapEncode;
 }
 
-template <int BNH, int EPI, typename TOut>
+template <int BNH, int EPI, typename TOut, bool FLUSH>
 int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
   using Cfg = TileCfg<BNH>;
-  auto kernel = col::sm100::gemm_bf16_tc_kernel<BNH, EPI, TOut>;
+  auto kernel = col::sm100::gemm_bf16_tc_kernel<BNH, EPI, TOut, FLUSH>;
   static std::atomic<std::uint64_t> attr_set{0};
   const std::uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set.load(std::memory_order_acquire) & bit)) {
@@ -115,10 +115,10 @@ int max_pair_clusters(int dev) {
   return cached[dev & 63];
 }
 
-template <int BNH, int EPI, typename TOut>
+template <int BNH, int EPI, typename TOut, bool FLUSH>
 int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
   using Cfg = col::sm100::TileCfg2<BNH>;
-  auto kernel = col::sm100::gemm_bf16_tc2_kernel<BNH, EPI, TOut>;
+  auto kernel = col::sm100::gemm_bf16_tc2_kernel<BNH, EPI, TOut, FLUSH>;
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int grid = 2 * (tiles < clusters ? tiles : clusters);
   kernel<<<grid, col::sm100::kCtaThreads, Cfg::kSmemBytes, s>>>(p);
@@ -126,13 +126,13 @@ int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
   return static_cast<int>(cudaGetLastError());
 }
 
-template <int BNH, int EPI, typename TOut>
+template <int BNH, int EPI, typename TOut, bool FLUSH>
 int set_smem_attr_2sm(int dev) {
   using Cfg = col::sm100::TileCfg2<BNH>;
   static std::atomic<std::uint64_t> attr_set{0};
   const std::uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set.load(std::memory_order_acquire) & bit)) {
-    const cudaError_t e = cudaFuncSetAttribute(col::sm100::gemm_bf16_tc2_kernel<BNH, EPI, TOut>,
+    const cudaError_t e = cudaFuncSetAttribute(col::sm100::gemm_bf16_tc2_kernel<BNH, EPI, TOut, FLUSH>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(Cfg::kSmemBytes));
     if (e != cudaSuccess) return static_cast<int>(e);
@@ -149,11 +149,13 @@ enum class BMode { kSwiGLU, kGelu };
 // so the cost of a choice is waves * 2*BNH.  Ties go to the wider tile (fewer
 // epilogues, better MMA efficiency).  Example: M=512, N=4096 SwiGLU gives 128
 // tiles at BNH=128 (one 86 %-full wave) but exactly 148 at BNH=112.
-int choose_bnh(int mblocks, std::uint64_t n, bool swiglu, int sm_count) {
+int choose_bnh(int mblocks, std::uint64_t n, bool swiglu, int sm_count, int max_bnh,
+               bool with112) {
   constexpr int kCandidates[] = {128, 112, 96, 64};
-  int best = 128;
+  int best = 64;
   std::uint64_t best_cost = ~0ull;
   for (int bnh : kCandidates) {
+    if (bnh > max_bnh || (bnh == 112 && !with112)) continue;
     const std::uint64_t cols = swiglu ? bnh : 2 * bnh;
     const std::uint64_t tiles = static_cast<std::uint64_t>(mblocks) * ((n + cols - 1) / cols);
     const std::uint64_t waves = (tiles + sm_count - 1) / sm_count;
@@ -166,16 +168,54 @@ int choose_bnh(int mblocks, std::uint64_t n, bool swiglu, int sm_count) {
   return best;
 }
 
-// bf16 tensor-core path.  For kSwiGLU, w0/w1 are the gate/up matrices [n, k];
-// for kGelu, w0 is W [n, k] (w1 ignored).  Returns -1 when TMA cannot address
-// the operands (caller falls back to the CUDA-core kernel).
-template <int EPI, typename TOut>
-int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, const float* bias,
-                 void* out, std::uint64_t m, std::uint64_t n, std::uint64_t k, cudaStream_t s) {
-  if ((k % 8) != 0 || !col::aligned16(x) || !col::aligned16(w0) ||
-      (mode == BMode::kSwiGLU && !col::aligned16(w1))) {
-    return -1;
+// fp32 emulation (below): k-blocks per flushed accumulation chunk of the a0*b0 segment (512 k): on
+// unit-scale data the max error against a float64 GEMM is ~5e-8 of
+// sum_k |x||w| at k = 4096, against ~7e-6 with one accumulation per tile.
+constexpr int kFlushKBlocks = 8;
+
+// Operands of one tensor-core launch: A [m, a_cols] bf16 (row stride a_cols)
+// and the two B maps [b_rows, b_cols] bf16 (SwiGLU: gate and up; GELU: W
+// twice).  k_blocks = number of 64-wide k-blocks; seg_* describe a segmented
+// K (fp32 emulation, below) or are 0.
+struct TcOperands {
+  const void* a;
+  std::uint64_t a_cols;
+  const void* b0;
+  const void* b1;
+  std::uint64_t b_rows;
+  std::uint64_t b_cols;
+  int k_blocks;
+  int seg_k_blocks;
+  std::uint32_t seg_pairs;
+};
+
+// Launch the tcgen05 kernel (CTA-pair when there are two or more 128-row
+// blocks).  Returns -1 when TMA cannot express the operands.
+// FLUSH (fp32 emulation) keeps a tile row's sums in registers, BNH floats a
+// thread.  Up to BNH = 96 they fit the 168 registers every thread gets; the
+// BNH = 128 kernels move registers from the control warpgroup to the
+// epilogue (setmaxnreg), which needs the kernel to have been compiled with
+// the full 168 a thread: checked once per kernel here, else BNH stops at 96.
+template <typename Kernel>
+bool launch_regs_cover_split(Kernel kernel) {
+  cudaFuncAttributes attr;
+  if (cudaFuncGetAttributes(&attr, kernel) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
   }
+  return attr.numRegs >= col::sm100::kRegsLaunchNeeded;
+}
+
+template <int EPI, typename TOut>
+bool flush_wide_ok(bool pair) {
+  static const bool one = launch_regs_cover_split(col::sm100::gemm_bf16_tc_kernel<128, EPI, TOut, true>);
+  static const bool two = launch_regs_cover_split(col::sm100::gemm_bf16_tc2_kernel<128, EPI, TOut, true>);
+  return pair ? two : one;
+}
+
+template <int EPI, typename TOut, bool FLUSH = false>
+int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, void* out,
+                       std::uint64_t m, std::uint64_t n, cudaStream_t s) {
   int dev = 0;
   const col::DeviceInfo& info = col::device_info(&dev);
   if (info.cc_major != 10) return col::kErrDeviceNotSupported;
@@ -188,19 +228,21 @@ int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, cons
   const bool pair = mblocks >= 2;
   int pair_slots = 0;
   if (pair) {
-    if (int rc = set_smem_attr_2sm<128, EPI, TOut>(dev)) return rc;
+    if (int rc = set_smem_attr_2sm<128, EPI, TOut, false>(dev)) return rc;
     pair_slots = max_pair_clusters<EPI, TOut>(dev);
   }
   const bool use_pair = pair && pair_slots > 0;
   const int mblocks_sched = use_pair ? (mblocks + 1) / 2 : mblocks;
+  int max_bnh = 128;
+  if constexpr (FLUSH) max_bnh = flush_wide_ok<EPI, TOut>(use_pair) ? 128 : 96;
   const int bnh = choose_bnh(mblocks_sched, n, mode == BMode::kSwiGLU,
-                             use_pair ? pair_slots : info.sm_count);
+                             use_pair ? pair_slots : info.sm_count, max_bnh, !FLUSH);
 
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
-  int rc = encode_bf16_rows(&p.map_a, x, m, k, 128);
-  if (rc == 0) rc = encode_bf16_rows(&p.map_b0, w0, n, k, bnh);
-  if (rc == 0) rc = encode_bf16_rows(&p.map_b1, mode == BMode::kSwiGLU ? w1 : w0, n, k, bnh);
+  int rc = encode_bf16_rows(&p.map_a, ops.a, m, ops.a_cols, 128);
+  if (rc == 0) rc = encode_bf16_rows(&p.map_b0, ops.b0, ops.b_rows, ops.b_cols, bnh);
+  if (rc == 0) rc = encode_bf16_rows(&p.map_b1, ops.b1, ops.b_rows, ops.b_cols, bnh);
   if (rc == col::kErrTensorMapEncode) return -1;  // layout TMA cannot express: CUDA cores
   if (rc != 0) return rc;
   p.bias = bias;
@@ -208,9 +250,11 @@ int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, cons
   p.status = status;
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
-  p.k = static_cast<int>(k);
+  p.k = static_cast<int>(ops.a_cols);
   p.num_m_blocks = mblocks_sched;
-  p.num_k_blocks = static_cast<int>((k + col::sm100::kBlockK - 1) / col::sm100::kBlockK);
+  p.num_k_blocks = ops.k_blocks;
+  p.seg_k_blocks = ops.seg_k_blocks;
+  p.seg_pairs = ops.seg_pairs;
   if (mode == BMode::kSwiGLU) {
     p.num_n_blocks = static_cast<int>((n + bnh - 1) / bnh);
     p.b_row_stride = bnh;
@@ -223,30 +267,162 @@ int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, cons
   // Few M-blocks per weight tile: the weights stream from DRAM with little L2
   // reuse, so warm L2 ahead of the ring.  Many M-blocks: the raster already
   // keeps each weight tile L2-resident across its M-group.
-  p.prefetch_b = mblocks <= 8 ? 1 : 0;
+  p.prefetch_b = (mblocks <= 8 && ops.seg_k_blocks == 0) ? 1 : 0;
   p.out_ld = static_cast<int>(n);
   p.out_vec_ok = col::aligned16(out) && ((n * sizeof(TOut)) % 16 == 0);
-  if (use_pair) {
-    int rc = 0;
+  p.flush_k_blocks = FLUSH ? kFlushKBlocks : 0;
+  if constexpr (FLUSH) {
+    if (use_pair) {
+      switch (bnh) {
+        case 128:
+          if ((rc = set_smem_attr_2sm<128, EPI, TOut, true>(dev))) return rc;
+          return launch_tc2<128, EPI, TOut, true>(p, s, dev, pair_slots);
+        case 96:
+          if ((rc = set_smem_attr_2sm<96, EPI, TOut, true>(dev))) return rc;
+          return launch_tc2<96, EPI, TOut, true>(p, s, dev, pair_slots);
+        default:
+          if ((rc = set_smem_attr_2sm<64, EPI, TOut, true>(dev))) return rc;
+          return launch_tc2<64, EPI, TOut, true>(p, s, dev, pair_slots);
+      }
+    }
+    switch (bnh) {  // choose_bnh offers 128, 96 and 64 only here
+      case 128: return launch_tc<128, EPI, TOut, true>(p, s, dev, info.sm_count);
+      case 96: return launch_tc<96, EPI, TOut, true>(p, s, dev, info.sm_count);
+      default: return launch_tc<64, EPI, TOut, true>(p, s, dev, info.sm_count);
+    }
+  } else {
+    if (use_pair) {
+      switch (bnh) {
+        case 128: return launch_tc2<128, EPI, TOut, false>(p, s, dev, pair_slots);
+        case 112:
+          if ((rc = set_smem_attr_2sm<112, EPI, TOut, false>(dev))) return rc;
+          return launch_tc2<112, EPI, TOut, false>(p, s, dev, pair_slots);
+        case 96:
+          if ((rc = set_smem_attr_2sm<96, EPI, TOut, false>(dev))) return rc;
+          return launch_tc2<96, EPI, TOut, false>(p, s, dev, pair_slots);
+        default:
+          if ((rc = set_smem_attr_2sm<64, EPI, TOut, false>(dev))) return rc;
+          return launch_tc2<64, EPI, TOut, false>(p, s, dev, pair_slots);
+      }
+    }
     switch (bnh) {
-      case 128: return launch_tc2<128, EPI, TOut>(p, s, dev, pair_slots);
-      case 112:
-        if ((rc = set_smem_attr_2sm<112, EPI, TOut>(dev))) return rc;
-        return launch_tc2<112, EPI, TOut>(p, s, dev, pair_slots);
-      case 96:
-        if ((rc = set_smem_attr_2sm<96, EPI, TOut>(dev))) return rc;
-        return launch_tc2<96, EPI, TOut>(p, s, dev, pair_slots);
-      default:
-        if ((rc = set_smem_attr_2sm<64, EPI, TOut>(dev))) return rc;
-        return launch_tc2<64, EPI, TOut>(p, s, dev, pair_slots);
+      case 128: return launch_tc<128, EPI, TOut, false>(p, s, dev, info.sm_count);
+      case 112: return launch_tc<112, EPI, TOut, false>(p, s, dev, info.sm_count);
+      case 96: return launch_tc<96, EPI, TOut, false>(p, s, dev, info.sm_count);
+      default: return launch_tc<64, EPI, TOut, false>(p, s, dev, info.sm_count);
     }
   }
-  switch (bnh) {
-    case 128: return launch_tc<128, EPI, TOut>(p, s, dev, info.sm_count);
-    case 112: return launch_tc<112, EPI, TOut>(p, s, dev, info.sm_count);
-    case 96: return launch_tc<96, EPI, TOut>(p, s, dev, info.sm_count);
-    default: return launch_tc<64, EPI, TOut>(p, s, dev, info.sm_count);
+}
+
+// bf16 operands straight from the caller: x [m, k], w0/w1 [n, k] (kGelu: w0 only).
+template <int EPI, typename TOut>
+int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, const float* bias,
+                 void* out, std::uint64_t m, std::uint64_t n, std::uint64_t k, cudaStream_t s) {
+  if ((k % 8) != 0 || !col::aligned16(x) || !col::aligned16(w0) ||
+      (mode == BMode::kSwiGLU && !col::aligned16(w1))) {
+    return -1;
   }
+  TcOperands ops{x, k, w0, mode == BMode::kSwiGLU ? w1 : w0, n, k,
+                 static_cast<int>((k + col::sm100::kBlockK - 1) / col::sm100::kBlockK), 0, 0u};
+  return launch_tensor_gemm<EPI, TOut>(ops, mode, bias, out, m, n, s);
+}
+
+// ---------------------------------------------------------------- fp32 on tensor cores
+//
+// An fp32 value a is split into three bf16 parts a = a0 + a1 + a2 + e with
+// a0 = bf16(a), a1 = bf16(a - a0), a2 = bf16(a - a0 - a1): 3 x 8 significand
+// bits, |e| <= 2^-24 |a|.  A product a.b is then the sum of the six part
+// products of total order <= 2 (a0b0, a0b1, a1b0, a1b1, a0b2, a2b0); the
+// three dropped ones are ~2^-23 |a||b|, the size of fp32 rounding.  bf16 x
+// bf16 products are exact in the tensor core's fp32 accumulator, so the GEMM
+// keeps fp32 accuracy while running on tcgen05: the parts are laid out side
+// by side along K ([a0 | a1 | a2], each part padded to a multiple of 64) and
+// one launch walks the six (A part, B part) segments.
+constexpr int kSplitSegments = 6;
+constexpr std::uint32_t kSplitPairs =
+    (0u << 0) | (0u << 2) |    // a0 b0
+    (0u << 4) | (1u << 6) |    // a0 b1
+    (1u << 8) | (0u << 10) |   // a1 b0
+    (1u << 12) | (1u << 14) |  // a1 b1
+    (0u << 16) | (2u << 18) |  // a0 b2
+    (2u << 20) | (0u << 22);   // a2 b0
+
+__global__ void __launch_bounds__(256)
+split_fp32_bf16x3_kernel(const float* __restrict__ src, std::uint64_t rows, std::uint32_t k,
+                         std::uint32_t kp, __nv_bfloat16* __restrict__ dst) {
+  // One thread per 8 consecutive k of one row: three 16-byte stores.
+  const std::uint64_t groups_per_row = kp / 8;
+  const std::uint64_t total = rows * groups_per_row;
+  for (std::uint64_t gi = static_cast<std::uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       gi < total; gi += static_cast<std::uint64_t>(gridDim.x) * blockDim.x) {
+    const std::uint64_t r = gi / groups_per_row;
+    const std::uint32_t k0 = static_cast<std::uint32_t>(gi - r * groups_per_row) * 8;
+    const float* row = src + r * k;
+    float p0[8], p1[8], p2[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float v = (k0 + j < k) ? __ldg(row + k0 + j) : 0.0f;
+      const float h = col::bf16_round(v);
+      const float r1 = v - h;
+      const float m = col::bf16_round(r1);
+      p0[j] = h;
+      p1[j] = m;
+      p2[j] = r1 - m;
+    }
+    uint4* out = reinterpret_cast<uint4*>(dst + r * (3ull * kp) + k0);
+    out[0] = col::pack_bf16x8(p0);
+    out[kp / 8] = col::pack_bf16x8(p1);
+    out[2 * (kp / 8)] = col::pack_bf16x8(p2);
+  }
+}
+
+int split_fp32(const float* src, std::uint64_t rows, std::uint64_t k, std::uint64_t kp,
+               __nv_bfloat16* dst, cudaStream_t s) {
+  const std::uint64_t work = rows * (kp / 8);
+  std::uint64_t blocks = (work + 255) / 256;
+  const std::uint64_t cap = static_cast<std::uint64_t>(col::device_info().sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks == 0) blocks = 1;
+  split_fp32_bf16x3_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+      src, rows, static_cast<std::uint32_t>(k), static_cast<std::uint32_t>(kp), dst);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// fp32 GEMM with fused epilogue on tensor cores.  kSwiGLU: w0/w1 are the gate
+// and up matrices [n, k] (for a packed weight, its two halves); kGelu: w0 is
+// W [n, k].  Scratch (the bf16 parts, 6 bytes per input element) comes from
+// the library's stream-ordered pool.  Returns -1 to request the CUDA-core path.
+template <int EPI>
+int gemm_fp32_tc(const float* x, const float* w0, const float* w1, BMode mode, const float* bias,
+                 float* out, std::uint64_t m, std::uint64_t n, std::uint64_t k, cudaStream_t s) {
+  if (col::device_info().cc_major != 10) return -1;
+  // Tiny problems: the split passes and the launch overheads would dominate.
+  if (static_cast<double>(m) * static_cast<double>(n) * static_cast<double>(k) < 4.0e6) return -1;
+  const std::uint64_t kp = (k + col::sm100::kBlockK - 1) / col::sm100::kBlockK * col::sm100::kBlockK;
+  const std::uint64_t b_rows = mode == BMode::kSwiGLU ? 2 * n : n;
+  const std::size_t a_bytes = static_cast<std::size_t>(m) * 3 * kp * 2;
+  const std::size_t b_bytes = static_cast<std::size_t>(b_rows) * 3 * kp * 2;
+  cudaMemPool_t pool = nullptr;
+  if (col::library_pool(&pool) != cudaSuccess) return -1;
+  void* scratch = nullptr;
+  if (cudaMallocFromPoolAsync(&scratch, a_bytes + b_bytes, pool, s) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  __nv_bfloat16* a3 = static_cast<__nv_bfloat16*>(scratch);
+  __nv_bfloat16* b3 = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(scratch) + a_bytes);
+  int rc = split_fp32(x, m, k, kp, a3, s);
+  if (rc == 0) rc = split_fp32(w0, n, k, kp, b3, s);
+  if (rc == 0 && mode == BMode::kSwiGLU) rc = split_fp32(w1, n, k, kp, b3 + n * 3 * kp, s);
+  if (rc == 0) {
+    const int seg_kb = static_cast<int>(kp / col::sm100::kBlockK);
+    TcOperands ops{a3, 3 * kp, b3, mode == BMode::kSwiGLU ? b3 + n * 3 * kp : b3, n, 3 * kp,
+                   kSplitSegments * seg_kb, seg_kb, kSplitPairs};
+    rc = launch_tensor_gemm<EPI, float, true>(ops, mode, bias, out, m, n, s);
+  }
+  const cudaError_t fe = cudaFreeAsync(scratch, s);
+  if (rc == 0 && fe != cudaSuccess) rc = static_cast<int>(fe);
+  return rc;
 }
 
 template <typename TIn, int EPI, typename TOut>
@@ -284,8 +460,11 @@ int swiglu_f32_dual(const float* x, const float* wg, const float* wu, const floa
   if (!x || !wg || !wu || !ws || !out || !dims_ok(m, n, k, 0x7fffffffull)) {
     return static_cast<int>(cudaErrorInvalidValue);
   }
-  return gemm_simt<float, col::sm100::kEpiSwiGLU, float>(x, wg, wu, nullptr, out, m, n, k,
-                                                        col::as_stream(stream));
+  const cudaStream_t s = col::as_stream(stream);
+  const int rc = gemm_fp32_tc<col::sm100::kEpiSwiGLU>(x, wg, wu, BMode::kSwiGLU, nullptr, out, m,
+                                                      n, k, s);
+  if (rc != -1) return rc;
+  return gemm_simt<float, col::sm100::kEpiSwiGLU, float>(x, wg, wu, nullptr, out, m, n, k, s);
 }
 
 // gemm_swiglu.cu:335-351: packed [2N, K]; n above INT32_MAX / 2 is invalid.
@@ -295,8 +474,12 @@ int swiglu_f32_packed(const float* x, const float* w, const float* ws, float* ou
   if (!x || !w || !ws || !out || !dims_ok(m, n, k, 0x7fffffffull / 2)) {
     return static_cast<int>(cudaErrorInvalidValue);
   }
-  return gemm_simt<float, col::sm100::kEpiSwiGLU, float>(
-      x, w, up_half(w, n, k, sizeof(float)), nullptr, out, m, n, k, col::as_stream(stream));
+  const cudaStream_t s = col::as_stream(stream);
+  const float* wu = static_cast<const float*>(up_half(w, n, k, sizeof(float)));
+  const int rc = gemm_fp32_tc<col::sm100::kEpiSwiGLU>(x, w, wu, BMode::kSwiGLU, nullptr, out, m,
+                                                      n, k, s);
+  if (rc != -1) return rc;
+  return gemm_simt<float, col::sm100::kEpiSwiGLU, float>(x, w, wu, nullptr, out, m, n, k, s);
 }
 
 template <int EPI>
@@ -307,7 +490,10 @@ int bias_gelu_f32(const float* x, const float* w, const float* b, float* out, st
   if (!x || !w || !b || !out || !dims_ok(m, n, k, 0x7fffffffull)) {
     return static_cast<int>(cudaErrorInvalidValue);
   }
-  return gemm_simt<float, EPI, float>(x, w, nullptr, b, out, m, n, k, col::as_stream(stream));
+  const cudaStream_t s = col::as_stream(stream);
+  const int rc = gemm_fp32_tc<EPI>(x, w, nullptr, BMode::kGelu, b, out, m, n, k, s);
+  if (rc != -1) return rc;
+  return gemm_simt<float, EPI, float>(x, w, nullptr, b, out, m, n, k, s);
 }
 
 // ---------------------------------------------------------------- bf16 GEMMs

@@ -75,7 +75,63 @@ struct __align__(64) GemmParams {
   int out_ld;         // output row stride in elements
   int out_vec_ok;     // 16-byte vector stores allowed
   int prefetch_b;     // issue L2 prefetches for B boxes ahead of the ring
+  // Segmented K (fp32 operands split into bf16 parts, see gemm.cu): when
+  // seg_k_blocks > 0 the k-loop runs over num_k_blocks = segments *
+  // seg_k_blocks blocks; segment s reads A from part (seg_pairs >> 4s) & 3
+  // and B from part (seg_pairs >> (4s + 2)) & 3, each part seg_k_blocks wide.
+  int seg_k_blocks;
+  uint32_t seg_pairs;
+  int flush_k_blocks;  // fp32 emulation: k-blocks per flushed chunk of segment 0
 };
+
+// Column (x) coordinates of k-block kb in A and in B.
+__device__ __forceinline__ void k_block_coords(const GemmParams& p, int kb, int& ax, int& bx) {
+  if (p.seg_k_blocks == 0) {
+    ax = bx = kb * kBlockK;
+    return;
+  }
+  const int seg = kb / p.seg_k_blocks;
+  const int local = kb - seg * p.seg_k_blocks;
+  const int a_part = static_cast<int>((p.seg_pairs >> (4 * seg)) & 3u);
+  const int b_part = static_cast<int>((p.seg_pairs >> (4 * seg + 2)) & 3u);
+  ax = (a_part * p.seg_k_blocks + local) * kBlockK;
+  bx = (b_part * p.seg_k_blocks + local) * kBlockK;
+}
+
+// Accumulation chunks of one tile.  The tensor core's fp32 accumulator adds
+// each K=16 step's products with truncation, so over thousands of k its
+// error grows to ~1e-5 of sum|a||b| -- harmless for bf16 outputs, too much for
+// the fp32 GEMMs.  With FLUSH the K loop is cut into chunks: segment 0 (the
+// a0*b0 products, the large ones) in chunks of flush_k_blocks k-blocks, then
+// one chunk for the remaining (2^-8 smaller) segments.  Each chunk restarts
+// the TMEM accumulator and the epilogue adds the chunk sums in registers with
+// round-to-nearest fp32 adds, which brings the error under fp32 rounding size.
+template <bool FLUSH>
+__device__ __forceinline__ int tile_chunks(const GemmParams& p) {
+  if constexpr (!FLUSH) {
+    return 1;
+  } else {
+    const int head = (p.seg_k_blocks + p.flush_k_blocks - 1) / p.flush_k_blocks;
+    return head + (p.num_k_blocks > p.seg_k_blocks ? 1 : 0);
+  }
+}
+
+template <bool FLUSH>
+__device__ __forceinline__ void chunk_range(const GemmParams& p, int c, int& kb0, int& kb1) {
+  if constexpr (!FLUSH) {
+    kb0 = 0;
+    kb1 = p.num_k_blocks;
+  } else {
+    const int head = (p.seg_k_blocks + p.flush_k_blocks - 1) / p.flush_k_blocks;
+    if (c < head) {
+      kb0 = c * p.flush_k_blocks;
+      kb1 = min(kb0 + p.flush_k_blocks, p.seg_k_blocks);
+    } else {
+      kb0 = p.seg_k_blocks;
+      kb1 = p.num_k_blocks;
+    }
+  }
+}
 
 constexpr uint32_t kSmemLimit = 232448;  // max dynamic shared memory per CTA on sm_100
 
@@ -191,6 +247,25 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Register split between warpgroups (setmaxnreg, whole warpgroup, aligned):
+// used by the FLUSH kernels with BNH = 128, whose epilogue holds 128 running
+// sums per thread.  Warpgroup 0 (producer, MMA, TMEM, idle warps) gives up
+// registers, the two epilogue warpgroups take them.  The shares must fit the
+// registers the CTA was launched with: 128 x kRegsControl + 256 x kRegsEpilogue
+// = 62464 <= 384 x 168 (the host checks the compiled count before launching).
+constexpr int kRegsControl = 56;
+constexpr int kRegsEpilogue = 216;
+constexpr int kRegsLaunchNeeded = (128 * kRegsControl + 32 * kEpiWarps * kRegsEpilogue + kCtaThreads - 1) / kCtaThreads;
+
+template <int N>
+__device__ __forceinline__ void regs_release() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_acquire() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -406,9 +481,81 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int row, int 
   }
 }
 
-// ------------------------------------------------------------ the kernel
+// Register sums for FLUSH: this thread's columns of one accumulator row.
+// Slot i covers accumulator columns c = group*16 + i*32 (16 wide; SwiGLU adds
+// the up columns BNH + c), so a thread holds BNH floats.
+template <int BNH, int EPI>
+struct ChunkSums {
+  static constexpr bool kSwiGLU = EPI == kEpiSwiGLU || EPI == kEpiSwiGLURoundBf16;
+  static constexpr int kLimit = kSwiGLU ? BNH : 2 * BNH;  // accumulator columns walked
+  static constexpr int kSlots = (kLimit + 16 * kEpiGroups - 1) / (16 * kEpiGroups);
+  static constexpr int kPerSlot = kSwiGLU ? 32 : 16;
+  float v[kSlots * kPerSlot];
+};
+
+template <int BNH, int EPI>
+__device__ __forceinline__ void accumulate_chunk(uint32_t t_row, int group, bool first,
+                                                 ChunkSums<BNH, EPI>& sums) {
+  using S = ChunkSums<BNH, EPI>;
+#pragma unroll
+  for (int i = 0; i < S::kSlots; ++i) {
+    const int c = group * 16 + i * 16 * kEpiGroups;
+    if (c < S::kLimit) {  // warp-uniform: group is per warp
+      float* dst = sums.v + i * S::kPerSlot;
+      if constexpr (S::kSwiGLU) {
+        uint32_t g[16], u[16];
+        tmem_ld16x2(t_row + c, t_row + BNH + c, g, u);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          dst[j] = first ? __uint_as_float(g[j]) : __fadd_rn(dst[j], __uint_as_float(g[j]));
+          dst[16 + j] = first ? __uint_as_float(u[j]) : __fadd_rn(dst[16 + j], __uint_as_float(u[j]));
+        }
+      } else {
+        uint32_t a[16];
+        tmem_ld16(t_row + c, a);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          dst[j] = first ? __uint_as_float(a[j]) : __fadd_rn(dst[j], __uint_as_float(a[j]));
+        }
+      }
+    }
+  }
+}
 
 template <int BNH, int EPI, typename TOut>
+__device__ __forceinline__ void epilogue_sums(const GemmParams& p, int row, int nb, int group,
+                                              const ChunkSums<BNH, EPI>& sums) {
+  using S = ChunkSums<BNH, EPI>;
+#pragma unroll
+  for (int i = 0; i < S::kSlots; ++i) {
+    const int c = group * 16 + i * 16 * kEpiGroups;
+    if (c < S::kLimit) {
+      const float* src = sums.v + i * S::kPerSlot;
+      float o[16];
+      if constexpr (S::kSwiGLU) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[j] = silu_f(src[j]) * src[16 + j];
+        store_chunk<TOut, 16>(p, row, nb * BNH + c, o);
+      } else {
+        const int col_base = nb * 2 * BNH + c;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float bv = col_base + j < p.n ? __ldg(p.bias + col_base + j) : 0.0f;
+          if constexpr (EPI == kEpiBiasGeluErf) {
+            o[j] = gelu_erf_f(src[j] + bv);
+          } else {
+            o[j] = gelu_tanh_f(src[j] + bv);
+          }
+        }
+        store_chunk<TOut, 16>(p, row, col_base, o);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------ the kernel
+
+template <int BNH, int EPI, typename TOut, bool FLUSH = false>
 __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
   using Cfg = TileCfg<BNH>;
   constexpr int kStages = Cfg::kStages;
@@ -449,142 +596,166 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-
   auto fail = [&](unsigned code) {
     atomicOr(p.status, code);
     *abort_flag = 1;
   };
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer
-      prefetch_tmap(&p.map_a);
-      prefetch_tmap(&p.map_b0);
-      prefetch_tmap(&p.map_b1);
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued_mask = 0;  // stages holding a copy that may be in flight
-      uint32_t issued_phase = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        int mb, nb;
-        tile_coords(tile, p, mb, nb);
-        const int a_row = mb * kBlockM;
-        const int b0_row = nb * p.b_row_stride;
-        const int b1_row = b0_row + p.b1_row_offset;
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1u, abort_flag)) {
-            fail(kStatusProducer);
-            ok = false;
-            break;
-          }
-          const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
-          const uint32_t sb = sa + Cfg::kABytes;
-          const uint32_t fb = smem_u32(full_bar + stage);
-          mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-          const int kx = kb * kBlockK;
-          tma_load_2d(sa, &p.map_a, fb, kx, a_row);
-          tma_load_2d(sb, &p.map_b0, fb, kx, b0_row);
-          tma_load_2d(sb + BNH * 128, &p.map_b1, fb, kx, b1_row);
-          // Weight boxes kPrefetchDepth k-blocks ahead go to L2 now, so when
-          // the ring reaches them the TMA reads hit L2 instead of waiting on
-          // DRAM (matters when few M-blocks share each weight tile).
-          if (p.prefetch_b && kb + kPrefetchDepth < p.num_k_blocks) {
-            const int px = kx + kPrefetchDepth * kBlockK;
-            tma_prefetch_l2_2d(&p.map_b0, px, b0_row);
-            tma_prefetch_l2_2d(&p.map_b1, px, b1_row);
-          }
-          issued_mask |= 1u << stage;
-          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
+  // Warpgroup 0: producer, MMA issuer, TMEM owner; warpgroups 1-2: epilogue.
+  if (warp < 4) {
+    if constexpr (FLUSH && BNH > 96) regs_release<kRegsControl>();
+    if (warp == 0) {
+      if (lane == 0) {
+        // ---------------- TMA producer
+        prefetch_tmap(&p.map_a);
+        prefetch_tmap(&p.map_b0);
+        prefetch_tmap(&p.map_b1);
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t issued_mask = 0;  // stages holding a copy that may be in flight
+        uint32_t issued_phase = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+          int mb, nb;
+          tile_coords(tile, p, mb, nb);
+          const int a_row = mb * kBlockM;
+          const int b0_row = nb * p.b_row_stride;
+          const int b1_row = b0_row + p.b1_row_offset;
+          for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+            if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1u, abort_flag)) {
+              fail(kStatusProducer);
+              ok = false;
+              break;
+            }
+            const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+            const uint32_t sb = sa + Cfg::kABytes;
+            const uint32_t fb = smem_u32(full_bar + stage);
+            mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
+            int ax, kx;
+            k_block_coords(p, kb, ax, kx);
+            tma_load_2d(sa, &p.map_a, fb, ax, a_row);
+            tma_load_2d(sb, &p.map_b0, fb, kx, b0_row);
+            tma_load_2d(sb + BNH * 128, &p.map_b1, fb, kx, b1_row);
+            // Weight boxes kPrefetchDepth k-blocks ahead go to L2 now, so when
+            // the ring reaches them the TMA reads hit L2 instead of waiting on
+            // DRAM (matters when few M-blocks share each weight tile).
+            if (p.prefetch_b && kb + kPrefetchDepth < p.num_k_blocks) {
+              const int px = kx + kPrefetchDepth * kBlockK;
+              tma_prefetch_l2_2d(&p.map_b0, px, b0_row);
+              tma_prefetch_l2_2d(&p.map_b1, px, b1_row);
+            }
+            issued_mask |= 1u << stage;
+            issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
         }
-      }
-      if (!ok || *abort_flag) {
-        // Drain: every copy this thread issued must land before the CTA exits.
-        for (int s = 0; s < kStages; ++s) {
-          if (issued_mask & (1u << s)) {
-            if (!mbar_wait_drain(smem_u32(full_bar + s), (issued_phase >> s) & 1u)) {
-              atomicOr(p.status, kStatusDrain);
+        if (!ok || *abort_flag) {
+          // Drain: every copy this thread issued must land before the CTA exits.
+          for (int s = 0; s < kStages; ++s) {
+            if (issued_mask & (1u << s)) {
+              if (!mbar_wait_drain(smem_u32(full_bar + s), (issued_phase >> s) & 1u)) {
+                atomicOr(p.status, kStatusDrain);
+              }
             }
           }
         }
       }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer
-      int stage = 0;
-      uint32_t phase = 0;
-      int local = 0;
-      bool ok = true;
-      bool issued_any = false;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1u, abort_flag)) {
-          fail(kStatusMma);
-          break;
+    } else if (warp == 1) {
+      if (lane == 0) {
+        // ---------------- MMA issuer
+        int stage = 0;
+        uint32_t phase = 0;
+        int local = 0;
+        bool ok = true;
+        bool issued_any = false;
+        const int chunks = tile_chunks<FLUSH>(p);
+        for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+          for (int c = 0; c < chunks; ++c, ++local) {
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1u, abort_flag)) {
+              fail(kStatusMma);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
+            int kb0, kb1;
+            chunk_range<FLUSH>(p, c, kb0, kb1);
+            for (int kb = kb0; kb < kb1; ++kb) {
+              if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
+                fail(kStatusMma);
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+              const uint32_t sb = sa + Cfg::kABytes;
+  #pragma unroll
+              for (int k = 0; k < kBlockK / 16; ++k) {
+                umma_bf16(d_tmem, sdesc_kmajor_sw128(sa + k * 32), sdesc_kmajor_sw128(sb + k * 32),
+                          kIdesc, (kb != kb0 || k != 0) ? 1u : 0u);
+              }
+              issued_any = true;
+              umma_commit(smem_u32(empty_bar + stage));
+              if (++stage == kStages) {
+                stage = 0;
+                phase ^= 1u;
+              }
+            }
+            if (!ok) break;
+            umma_commit(smem_u32(tfull_bar + acc));
+          }
         }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
-            fail(kStatusMma);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
-          const uint32_t sb = sa + Cfg::kABytes;
-#pragma unroll
-          for (int k = 0; k < kBlockK / 16; ++k) {
-            umma_bf16(d_tmem, sdesc_kmajor_sw128(sa + k * 32), sdesc_kmajor_sw128(sb + k * 32),
-                      kIdesc, (kb | k) != 0 ? 1u : 0u);
-          }
-          issued_any = true;
-          umma_commit(smem_u32(empty_bar + stage));
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
+        // All MMAs this thread issued must finish before TMEM is released.
+        if (issued_any) {
+          umma_commit(smem_u32(drain_bar));
+          if (!mbar_wait_drain(smem_u32(drain_bar), 0)) atomicOr(p.status, kStatusDrain);
         }
-        if (!ok) break;
-        umma_commit(smem_u32(tfull_bar + acc));
-      }
-      // All MMAs this thread issued must finish before TMEM is released.
-      if (issued_any) {
-        umma_commit(smem_u32(drain_bar));
-        if (!mbar_wait_drain(smem_u32(drain_bar), 0)) atomicOr(p.status, kStatusDrain);
       }
     }
-  } else if (warp >= 4) {
+  } else {
+    if constexpr (FLUSH && BNH > 96) regs_acquire<kRegsEpilogue>();
     // ---------------- epilogue: warp w owns TMEM lanes [32q, 32q + 32) with
     // q = w % 4; the kEpiGroups warps of a quarter split its columns.
     const int q = warp & 3;
     const int group = (warp - 4) >> 2;
+    const int chunks = tile_chunks<FLUSH>(p);
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
-      // All lanes wait, then agree, so the warp-collective tcgen05.ld below
-      // always runs with the full warp.
-      const bool got = mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag);
-      if (!__all_sync(0xffffffffu, got)) {
-        if (lane == 0) fail(kStatusEpilogue);
-        break;
-      }
-      tc_fence_after();
       const int row = mb * kBlockM + q * 32 + lane;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccStride;
-      epilogue_tile<BNH, EPI, TOut>(p, row, nb, t_row, group);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(tempty_bar + acc));
+      ChunkSums<BNH, EPI> sums;
+      for (int c = 0; c < chunks; ++c, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        // All lanes wait, then agree, so the warp-collective tcgen05.ld below
+        // always runs with the full warp.
+        const bool got = mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag);
+        if (!__all_sync(0xffffffffu, got)) {
+          if (lane == 0) fail(kStatusEpilogue);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccStride;
+        if constexpr (FLUSH) {
+          accumulate_chunk<BNH, EPI>(t_row, group, c == 0, sums);
+        } else {
+          epilogue_tile<BNH, EPI, TOut>(p, row, nb, t_row, group);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(tempty_bar + acc));
+      }
+      if constexpr (FLUSH) {
+        if (ok) epilogue_sums<BNH, EPI, TOut>(p, row, nb, group, sums);
+      }
     }
   }
 

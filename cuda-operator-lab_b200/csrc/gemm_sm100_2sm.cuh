@@ -115,7 +115,7 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols)
 }
 
 // Pair tiles: p.num_m_blocks counts 256-row pair blocks here.
-template <int BNH, int EPI, typename TOut>
+template <int BNH, int EPI, typename TOut, bool FLUSH = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ GemmParams p) {
   using Cfg = TileCfg2<BNH>;
@@ -160,138 +160,163 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-
   auto fail = [&](unsigned code) {
     atomicOr(p.status, code);
     *abort_flag = 1;
   };
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer (both CTAs)
-      prefetch_tmap(&p.map_a);
-      prefetch_tmap(leader ? &p.map_b0 : &p.map_b1);
-      const CUtensorMap* map_b = leader ? &p.map_b0 : &p.map_b1;
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued_mask = 0;
-      uint32_t issued_phase = 0;
-      bool ok = true;
-      for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
-        int mb, nb;
-        tile_coords(tile, p, mb, nb);
-        const int a_row = mb * Cfg::kMmaM + static_cast<int>(rank) * kBlockM;
-        // SwiGLU: both CTAs use row nb*BNH (of the gate map / the up map);
-        // GELU: CTA r loads rows nb*2*BNH + r*BNH of W.
-        const int b_row = nb * p.b_row_stride + static_cast<int>(rank) * p.b1_row_offset;
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1u, abort_flag)) {
-            fail(kStatusProducer);
-            ok = false;
-            break;
-          }
-          const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
-          const uint32_t sb = sa + Cfg::kABytes;
-          const uint32_t fb_local = smem_u32(full_bar + stage);
-          if (leader) mbar_arrive_expect_tx(fb_local, 2 * Cfg::kStageBytes);
-          const uint32_t fb = map_to_cta(fb_local, 0);
-          const int kx = kb * kBlockK;
-          tma_load_2d_pair(sa, &p.map_a, fb, kx, a_row);
-          tma_load_2d_pair(sb, map_b, fb, kx, b_row);
-          if (p.prefetch_b && kb + kPrefetchDepth < p.num_k_blocks) {
-            tma_prefetch_l2_2d(map_b, kx + kPrefetchDepth * kBlockK, b_row);
-          }
-          issued_mask |= 1u << stage;
-          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
-      if (!ok || *abort_flag) {
-        if (leader) {
-          for (int s = 0; s < kStages; ++s) {
-            if (issued_mask & (1u << s)) {
-              if (!mbar_wait_drain(smem_u32(full_bar + s), (issued_phase >> s) & 1u)) {
-                atomicOr(p.status, kStatusDrain);
-              }
+  // Warpgroup 0: producer, MMA issuer, TMEM owner; warpgroups 1-2: epilogue.
+  if (warp < 4) {
+    if constexpr (FLUSH && BNH > 96) regs_release<kRegsControl>();
+    if (warp == 0) {
+      if (lane == 0) {
+        // ---------------- TMA producer (both CTAs)
+        prefetch_tmap(&p.map_a);
+        prefetch_tmap(leader ? &p.map_b0 : &p.map_b1);
+        const CUtensorMap* map_b = leader ? &p.map_b0 : &p.map_b1;
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t issued_mask = 0;
+        uint32_t issued_phase = 0;
+        bool ok = true;
+        for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+          int mb, nb;
+          tile_coords(tile, p, mb, nb);
+          const int a_row = mb * Cfg::kMmaM + static_cast<int>(rank) * kBlockM;
+          // SwiGLU: both CTAs use row nb*BNH (of the gate map / the up map);
+          // GELU: CTA r loads rows nb*2*BNH + r*BNH of W.
+          const int b_row = nb * p.b_row_stride + static_cast<int>(rank) * p.b1_row_offset;
+          for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+            if (!mbar_wait(smem_u32(empty_bar + stage), phase ^ 1u, abort_flag)) {
+              fail(kStatusProducer);
+              ok = false;
+              break;
+            }
+            const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+            const uint32_t sb = sa + Cfg::kABytes;
+            const uint32_t fb_local = smem_u32(full_bar + stage);
+            if (leader) mbar_arrive_expect_tx(fb_local, 2 * Cfg::kStageBytes);
+            const uint32_t fb = map_to_cta(fb_local, 0);
+            int ax, kx;
+            k_block_coords(p, kb, ax, kx);
+            tma_load_2d_pair(sa, &p.map_a, fb, ax, a_row);
+            tma_load_2d_pair(sb, map_b, fb, kx, b_row);
+            if (p.prefetch_b && kb + kPrefetchDepth < p.num_k_blocks) {
+              tma_prefetch_l2_2d(map_b, kx + kPrefetchDepth * kBlockK, b_row);
+            }
+            issued_mask |= 1u << stage;
+            issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
             }
           }
-        } else {
-          // CTA 1 cannot observe CTA 0's barrier: give its copies time to land.
-          for (int i = 0; i < 200; ++i) __nanosleep(1000);
+        }
+        if (!ok || *abort_flag) {
+          if (leader) {
+            for (int s = 0; s < kStages; ++s) {
+              if (issued_mask & (1u << s)) {
+                if (!mbar_wait_drain(smem_u32(full_bar + s), (issued_phase >> s) & 1u)) {
+                  atomicOr(p.status, kStatusDrain);
+                }
+              }
+            }
+          } else {
+            // CTA 1 cannot observe CTA 0's barrier: give its copies time to land.
+            for (int i = 0; i < 200; ++i) __nanosleep(1000);
+          }
+        }
+      }
+    } else if (warp == 1) {
+      if (lane == 0 && leader) {
+        // ---------------- MMA issuer (CTA 0 only)
+        int stage = 0;
+        uint32_t phase = 0;
+        int local = 0;
+        bool ok = true;
+        bool issued_any = false;
+        const int chunks = tile_chunks<FLUSH>(p);
+        for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+          for (int c = 0; c < chunks; ++c, ++local) {
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1u, abort_flag)) {
+              fail(kStatusMma);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
+            int kb0, kb1;
+            chunk_range<FLUSH>(p, c, kb0, kb1);
+            for (int kb = kb0; kb < kb1; ++kb) {
+              if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
+                fail(kStatusMma);
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
+              const uint32_t sb = sa + Cfg::kABytes;
+  #pragma unroll
+              for (int k = 0; k < kBlockK / 16; ++k) {
+                umma_bf16_pair(d_tmem, sdesc_kmajor_sw128(sa + k * 32),
+                               sdesc_kmajor_sw128(sb + k * 32), kIdesc,
+                               (kb != kb0 || k != 0) ? 1u : 0u);
+              }
+              issued_any = true;
+              umma_commit_pair_both(smem_u32(empty_bar + stage));
+              if (++stage == kStages) {
+                stage = 0;
+                phase ^= 1u;
+              }
+            }
+            if (!ok) break;
+            umma_commit_pair_both(smem_u32(tfull_bar + acc));
+          }
+        }
+        if (issued_any) {
+          umma_commit_pair_local(smem_u32(drain_bar));
+          if (!mbar_wait_drain(smem_u32(drain_bar), 0)) atomicOr(p.status, kStatusDrain);
         }
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0 && leader) {
-      // ---------------- MMA issuer (CTA 0 only)
-      int stage = 0;
-      uint32_t phase = 0;
-      int local = 0;
-      bool ok = true;
-      bool issued_any = false;
-      for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(smem_u32(tempty_bar + acc), acc_phase ^ 1u, abort_flag)) {
-          fail(kStatusMma);
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
-            fail(kStatusMma);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
-          const uint32_t sb = sa + Cfg::kABytes;
-#pragma unroll
-          for (int k = 0; k < kBlockK / 16; ++k) {
-            umma_bf16_pair(d_tmem, sdesc_kmajor_sw128(sa + k * 32), sdesc_kmajor_sw128(sb + k * 32),
-                           kIdesc, (kb | k) != 0 ? 1u : 0u);
-          }
-          issued_any = true;
-          umma_commit_pair_both(smem_u32(empty_bar + stage));
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (!ok) break;
-        umma_commit_pair_both(smem_u32(tfull_bar + acc));
-      }
-      if (issued_any) {
-        umma_commit_pair_local(smem_u32(drain_bar));
-        if (!mbar_wait_drain(smem_u32(drain_bar), 0)) atomicOr(p.status, kStatusDrain);
-      }
-    }
-  } else if (warp >= 4) {
+  } else {
+    if constexpr (FLUSH && BNH > 96) regs_acquire<kRegsEpilogue>();
     // ---------------- epilogue (both CTAs): this CTA's 128 rows of the tile
     const int q = warp & 3;
     const int group = (warp - 4) >> 2;
+    const int chunks = tile_chunks<FLUSH>(p);
     int local = 0;
-    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+    bool ok = true;
+    for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
       int mb, nb;
       tile_coords(tile, p, mb, nb);
-      const bool got = mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag);
-      if (!__all_sync(0xffffffffu, got)) {
-        if (lane == 0) fail(kStatusEpilogue);
-        break;
-      }
-      tc_fence_after();
       const int row = mb * Cfg::kMmaM + static_cast<int>(rank) * kBlockM + q * 32 + lane;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccStride;
-      epilogue_tile<BNH, EPI, TOut>(p, row, nb, t_row, group);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(tempty_bar + acc), 0));
+      ChunkSums<BNH, EPI> sums;
+      for (int c = 0; c < chunks; ++c, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        const bool got = mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag);
+        if (!__all_sync(0xffffffffu, got)) {
+          if (lane == 0) fail(kStatusEpilogue);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccStride;
+        if constexpr (FLUSH) {
+          accumulate_chunk<BNH, EPI>(t_row, group, c == 0, sums);
+        } else {
+          epilogue_tile<BNH, EPI, TOut>(p, row, nb, t_row, group);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(tempty_bar + acc), 0));
+      }
+      if constexpr (FLUSH) {
+        if (ok) epilogue_sums<BNH, EPI, TOut>(p, row, nb, group, sums);
+      }
     }
   }
 

@@ -24,29 +24,31 @@ __global__ void __launch_bounds__(kThreads)
 swiglu_vec_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
                   float4* __restrict__ o, std::uint64_t nvec) {
   const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
-  std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
+  // Groups of kUnroll strided vectors, the last group predicated, so the
+  // ragged end costs one memory round trip like every other group.
+  for (std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x; i < nvec;
+       i += kUnroll * stride) {
     float4 gv[kUnroll], uv[kUnroll];
 #pragma unroll
     for (int j = 0; j < kUnroll; ++j) {
-      gv[j] = col::ld_stream_f4(g + i + j * stride);
-      uv[j] = col::ld_stream_f4(u + i + j * stride);
+      const std::uint64_t idx = i + j * stride;
+      if (idx < nvec) {
+        gv[j] = col::ld_stream_f4(g + idx);
+        uv[j] = col::ld_stream_f4(u + idx);
+      }
     }
 #pragma unroll
     for (int j = 0; j < kUnroll; ++j) {
-      float4 r;
-      r.x = col::silu_f(gv[j].x) * uv[j].x;
-      r.y = col::silu_f(gv[j].y) * uv[j].y;
-      r.z = col::silu_f(gv[j].z) * uv[j].z;
-      r.w = col::silu_f(gv[j].w) * uv[j].w;
-      col::st_stream_f4(o + i + j * stride, r);
+      const std::uint64_t idx = i + j * stride;
+      if (idx < nvec) {
+        float4 r;
+        r.x = col::silu_f(gv[j].x) * uv[j].x;
+        r.y = col::silu_f(gv[j].y) * uv[j].y;
+        r.z = col::silu_f(gv[j].z) * uv[j].z;
+        r.w = col::silu_f(gv[j].w) * uv[j].w;
+        col::st_stream_f4(o + idx, r);
+      }
     }
-  }
-  for (; i < nvec; i += stride) {
-    const float4 gv = col::ld_stream_f4(g + i);
-    const float4 uv = col::ld_stream_f4(u + i);
-    col::st_stream_f4(o + i, make_float4(col::silu_f(gv.x) * uv.x, col::silu_f(gv.y) * uv.y,
-                                         col::silu_f(gv.z) * uv.z, col::silu_f(gv.w) * uv.w));
   }
 }
 
@@ -90,28 +92,25 @@ bias_gelu_vec_kernel(const float4* __restrict__ x, const float4* __restrict__ b,
   if (c >= vcols) return;
   const float4 bv = __ldg(b + c);
   const std::uint32_t rstride = gridDim.y;
-  std::uint32_t r = blockIdx.y;
-  for (; r + (kUnroll - 1) * rstride < rows; r += kUnroll * rstride) {
+  for (std::uint32_t r = blockIdx.y; r < rows; r += kUnroll * rstride) {
     float4 xv[kUnroll];
 #pragma unroll
     for (int j = 0; j < kUnroll; ++j) {
-      xv[j] = col::ld_stream_f4(x + static_cast<std::uint64_t>(r + j * rstride) * vcols + c);
+      const std::uint32_t rr = r + j * rstride;
+      if (rr < rows) xv[j] = col::ld_stream_f4(x + static_cast<std::uint64_t>(rr) * vcols + c);
     }
 #pragma unroll
     for (int j = 0; j < kUnroll; ++j) {
-      float4 v;
-      v.x = col::gelu_erf_f(xv[j].x + bv.x);
-      v.y = col::gelu_erf_f(xv[j].y + bv.y);
-      v.z = col::gelu_erf_f(xv[j].z + bv.z);
-      v.w = col::gelu_erf_f(xv[j].w + bv.w);
-      col::st_stream_f4(o + static_cast<std::uint64_t>(r + j * rstride) * vcols + c, v);
+      const std::uint32_t rr = r + j * rstride;
+      if (rr < rows) {
+        float4 v;
+        v.x = col::gelu_erf_f(xv[j].x + bv.x);
+        v.y = col::gelu_erf_f(xv[j].y + bv.y);
+        v.z = col::gelu_erf_f(xv[j].z + bv.z);
+        v.w = col::gelu_erf_f(xv[j].w + bv.w);
+        col::st_stream_f4(o + static_cast<std::uint64_t>(rr) * vcols + c, v);
+      }
     }
-  }
-  for (; r < rows; r += rstride) {
-    const std::uint64_t i = static_cast<std::uint64_t>(r) * vcols + c;
-    const float4 xv = col::ld_stream_f4(x + i);
-    col::st_stream_f4(o + i, make_float4(col::gelu_erf_f(xv.x + bv.x), col::gelu_erf_f(xv.y + bv.y),
-                                         col::gelu_erf_f(xv.z + bv.z), col::gelu_erf_f(xv.w + bv.w)));
   }
 }
 

@@ -1,7 +1,7 @@
 // Global sum of an fp32 vector (reduction.cuh:8-44).
 //
 // The input is split into G equal chunks (G <= 8 x SM count, one resident
-// wave); CTA b sums chunk b in fp64 (16-byte streaming loads, four
+// wave); CTA b sums chunk b in fp64 (16-byte streaming loads, eight
 // independent vectors in flight per thread), writes its partial to a scratch
 // slot, and the CTA that finishes last adds the G partials in index order.
 // The partition and the combine order depend only on n and the SM count, so
@@ -13,9 +13,47 @@
 
 #include "common.cuh"
 
+namespace col {
+
+// Library-owned stream-ordered memory pool of the current device.  Its
+// release threshold keeps freed blocks mapped, so the per-call scratch
+// allocation below is a cheap pool hit instead of a fresh mapping after
+// every synchronisation (what the default pool, threshold 0, would do).
+// Shared by every operator that needs stream-ordered scratch.
+cudaError_t library_pool(cudaMemPool_t* pool) {
+  constexpr int kMaxDevices = 64;
+  static cudaMemPool_t pools[kMaxDevices] = {};
+  static cudaError_t errors[kMaxDevices] = {};
+  static std::once_flag flags[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::call_once(flags[dev], [dev]() {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t p = nullptr;
+    cudaError_t err = cudaMemPoolCreate(&p, &props);
+    if (err == cudaSuccess) {
+      std::uint64_t keep = ~0ull;
+      err = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    pools[dev] = p;
+    errors[dev] = err;
+  });
+  *pool = pools[dev];
+  return errors[dev];
+}
+
+}  // namespace col
+
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kUnroll = 8;  // 16-byte loads in flight per thread
 constexpr int kCtasPerSm = 8;                   // fallback: 256-thread CTAs per SM
 constexpr std::uint64_t kChunkQuantum = 1024;   // elements: one float4 per thread
 constexpr std::uint64_t kMinChunk = 4096;
@@ -92,28 +130,25 @@ sum_kernel(const float* __restrict__ x, std::uint64_t n, std::uint64_t per_cta,
   if constexpr (VEC) {
     const float4* __restrict__ xv = reinterpret_cast<const float4*>(x + begin);
     const std::uint64_t nv = (end - begin) / 4;
-    std::uint64_t i = threadIdx.x;
-    for (; i + 3 * kThreads < nv; i += 4 * kThreads) {
-      float4 q[4];
+    // Groups of kUnroll strided vectors, the last group predicated: every
+    // group costs one memory round trip, including the ragged end.
+    for (std::uint64_t i = threadIdx.x; i < nv; i += kUnroll * kThreads) {
+      float4 q[kUnroll];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) q[j] = col::ld_stream_f4(xv + i + j * kThreads);
+      for (int j = 0; j < kUnroll; ++j) {
+        const std::uint64_t idx = i + static_cast<std::uint64_t>(j) * kThreads;
+        q[j] = idx < nv ? col::ld_stream_f4(xv + idx) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < kUnroll; ++j) {
         acc += static_cast<double>(q[j].x);
         acc += static_cast<double>(q[j].y);
         acc += static_cast<double>(q[j].z);
         acc += static_cast<double>(q[j].w);
       }
     }
-    for (; i < nv; i += kThreads) {
-      const float4 q = col::ld_stream_f4(xv + i);
-      acc += static_cast<double>(q.x);
-      acc += static_cast<double>(q.y);
-      acc += static_cast<double>(q.z);
-      acc += static_cast<double>(q.w);
-    }
     for (std::uint64_t k = begin + nv * 4 + threadIdx.x; k < end; k += kThreads) {
-      acc += static_cast<double>(x[k]);
+      acc += static_cast<double>(x[k]);  // at most 3 trailing elements
     }
   } else {
     for (std::uint64_t k = begin + threadIdx.x; k < end; k += kThreads) {
@@ -158,38 +193,6 @@ int launch_sum(const float* x, void* out, std::uint64_t n, cudaStream_t s, doubl
   return static_cast<int>(cudaGetLastError());
 }
 
-// Library-owned stream-ordered memory pool of the current device.  Its
-// release threshold keeps freed blocks mapped, so the per-call scratch
-// allocation below is a cheap pool hit instead of a fresh mapping after
-// every synchronisation (what the default pool, threshold 0, would do).
-cudaError_t scratch_pool(cudaMemPool_t* pool) {
-  constexpr int kMaxDevices = 64;
-  static cudaMemPool_t pools[kMaxDevices] = {};
-  static cudaError_t errors[kMaxDevices] = {};
-  static std::once_flag flags[kMaxDevices];
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  std::call_once(flags[dev], [dev]() {
-    cudaMemPoolProps props = {};
-    props.allocType = cudaMemAllocationTypePinned;
-    props.handleTypes = cudaMemHandleTypeNone;
-    props.location.type = cudaMemLocationTypeDevice;
-    props.location.id = dev;
-    cudaMemPool_t p = nullptr;
-    cudaError_t err = cudaMemPoolCreate(&p, &props);
-    if (err == cudaSuccess) {
-      std::uint64_t keep = ~0ull;
-      err = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
-    }
-    pools[dev] = p;
-    errors[dev] = err;
-  });
-  *pool = pools[dev];
-  return errors[dev];
-}
-
 // Stream-ordered scratch: allocated and freed on the caller's stream, so
 // concurrent calls on different streams never share it.
 template <bool OUT_F64>
@@ -197,7 +200,7 @@ int reduce_with_pool_scratch(const float* x, void* out, std::uint64_t n, cudaStr
   const Plan p = plan_for(n);
   const std::size_t bytes = static_cast<std::size_t>(p.ctas) * sizeof(double) + 16;
   cudaMemPool_t pool = nullptr;
-  cudaError_t st = scratch_pool(&pool);
+  cudaError_t st = col::library_pool(&pool);
   if (st != cudaSuccess) return static_cast<int>(st);
   void* scratch = nullptr;
   st = cudaMallocFromPoolAsync(&scratch, bytes, pool, s);
@@ -212,13 +215,84 @@ int reduce_with_pool_scratch(const float* x, void* out, std::uint64_t n, cudaStr
   return rc;
 }
 
+// Persistent scratch per (device, stream): sized once for the largest plan
+// (one wave of CTAs), counter zeroed once when it is created and put back
+// to zero by the finishing CTA of every launch.  Work on one stream is
+// ordered, and different streams get different blocks, so the counter is
+// zero whenever a launch starts and a call is a single kernel launch.  The
+// block is created on the first call on a stream (cudaMalloc plus a memset
+// on that stream); a stream that is being captured into a graph, or more
+// than kMaxStreamScratch streams, use the stream-ordered pool path instead.
+constexpr int kMaxStreamScratch = 256;
+
+struct StreamScratch {
+  int device;
+  cudaStream_t stream;
+  double* partials;
+  unsigned* counter;
+};
+
+bool stream_scratch(cudaStream_t s, unsigned ctas, double** partials, unsigned** counter) {
+  static std::mutex mu;
+  static StreamScratch entries[kMaxStreamScratch];
+  static int used = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const unsigned capacity = static_cast<unsigned>(col::device_info().sm_count) *
+                            static_cast<unsigned>(resident_ctas_per_sm());
+  if (ctas > capacity) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i) {
+    if (entries[i].device == dev && entries[i].stream == s) {
+      *partials = entries[i].partials;
+      *counter = entries[i].counter;
+      return true;
+    }
+  }
+  if (used == kMaxStreamScratch) return false;
+  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &capturing) != cudaSuccess ||
+      capturing != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return false;
+  }
+  void* block = nullptr;
+  const std::size_t bytes = static_cast<std::size_t>(capacity) * sizeof(double) + 256;
+  if (cudaMalloc(&block, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  double* p = static_cast<double*>(block);
+  unsigned* c = reinterpret_cast<unsigned*>(p + capacity);
+  if (cudaMemsetAsync(c, 0, sizeof(unsigned), s) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(block);
+    return false;
+  }
+  entries[used++] = StreamScratch{dev, s, p, c};
+  *partials = p;
+  *counter = c;
+  return true;
+}
+
+template <bool OUT_F64>
+int reduce_any(const float* x, void* out, std::uint64_t n, cudaStream_t s) {
+  const Plan p = plan_for(n);
+  double* partials = nullptr;
+  unsigned* counter = nullptr;
+  if (stream_scratch(s, p.ctas, &partials, &counter)) {
+    return launch_sum<OUT_F64>(x, out, n, s, partials, counter);
+  }
+  return reduce_with_pool_scratch<OUT_F64>(x, out, n, s);
+}
+
 // reduction.cu:160-167 and :179-181: output NULL, or input NULL with n > 0,
 // is cudaErrorInvalidValue; n == 0 writes 0.
 int reduce_f32(const float* x, float* out, std::uint64_t n, void* stream) {
   if (out == nullptr || (x == nullptr && n != 0)) return static_cast<int>(cudaErrorInvalidValue);
   const cudaStream_t s = col::as_stream(stream);
   if (n == 0) return static_cast<int>(cudaMemsetAsync(out, 0, sizeof(float), s));
-  return reduce_with_pool_scratch<false>(x, out, n, s);
+  return reduce_any<false>(x, out, n, s);
 }
 
 }  // namespace
@@ -249,7 +323,7 @@ COL_API int cuda_operator_reduction_partial_f64(const float* input, double* part
   }
   const cudaStream_t s = col::as_stream(stream);
   if (n == 0) return static_cast<int>(cudaMemsetAsync(partial, 0, sizeof(double), s));
-  return reduce_with_pool_scratch<true>(input, partial, n, s);
+  return reduce_any<true>(input, partial, n, s);
 }
 
 // ============================================================================

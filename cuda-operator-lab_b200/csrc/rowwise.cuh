@@ -182,6 +182,17 @@ row_kernel(const RowArgs a) {
   const float inv_cols = 1.0f / static_cast<float>(cols);
 
   if constexpr (OP == RowOp::kRms) {
+    // Weights are loaded before the reduction so their latency overlaps it
+    // (when the registers allow: up to 16 elements per thread).
+    constexpr bool kEarly = NV * VEC <= 16;
+    const T* __restrict__ w = static_cast<const T*>(a.weight);
+    float wv[kEarly ? NV : 1][VEC];
+    if constexpr (kEarly) {
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        if (ok[j]) load_param<T, VEC>(w + (static_cast<std::uint32_t>(j) * TPR + t) * VEC, wv[j]);
+      }
+    }
     float s = 0.0f;
 #pragma unroll
     for (int j = 0; j < NV; ++j)
@@ -189,19 +200,40 @@ row_kernel(const RowArgs a) {
       for (int e = 0; e < VEC; ++e) s = fmaf(v[j][e], v[j][e], s);
     s = group_sum<TPR>(s, sh);
     const float rstd = rsqrtf(s * inv_cols + a.eps);
-    const T* __restrict__ w = static_cast<const T*>(a.weight);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       if (ok[j]) {
         const std::uint32_t idx = (static_cast<std::uint32_t>(j) * TPR + t) * VEC;
-        float wv[VEC], o[VEC];
-        load_param<T, VEC>(w + idx, wv);
+        float o[VEC];
+        if constexpr (kEarly) {
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = (v[j][e] * rstd) * wv[e];
+          for (int e = 0; e < VEC; ++e) o[e] = (v[j][e] * rstd) * wv[j][e];
+        } else {
+          float wl[VEC];
+          load_param<T, VEC>(w + idx, wl);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) o[e] = (v[j][e] * rstd) * wl[e];
+        }
         store_vec<T, VEC>(y + idx, o);
       }
     }
   } else if constexpr (OP == RowOp::kLayerNorm || OP == RowOp::kResidualLayerNorm) {
+    // gamma/beta are loaded before the reductions so their latency overlaps
+    // them (when the registers allow: up to 16 elements per thread).
+    constexpr bool kEarly = NV * VEC <= 16;
+    const T* __restrict__ g = static_cast<const T*>(a.weight);
+    const T* __restrict__ b = static_cast<const T*>(a.bias);
+    float gv[kEarly ? NV : 1][VEC], bv[kEarly ? NV : 1][VEC];
+    if constexpr (kEarly) {
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        if (ok[j]) {
+          const std::uint32_t idx = (static_cast<std::uint32_t>(j) * TPR + t) * VEC;
+          load_param<T, VEC>(g + idx, gv[j]);
+          load_param<T, VEC>(b + idx, bv[j]);
+        }
+      }
+    }
     // Shifted sum: subtracting the row's first element (the same value in
     // every thread of the row) keeps the partial sums small when the row
     // carries a large common offset, so the mean keeps its low-order bits.
@@ -234,17 +266,21 @@ row_kernel(const RowArgs a) {
     }
     const float var = group_sum<TPR>(q, sh) * inv_cols;
     const float rstd = rsqrtf(var + a.eps);
-    const T* __restrict__ g = static_cast<const T*>(a.weight);
-    const T* __restrict__ b = static_cast<const T*>(a.bias);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       if (ok[j]) {
         const std::uint32_t idx = (static_cast<std::uint32_t>(j) * TPR + t) * VEC;
-        float gv[VEC], bv[VEC], o[VEC];
-        load_param<T, VEC>(g + idx, gv);
-        load_param<T, VEC>(b + idx, bv);
+        float o[VEC];
+        if constexpr (kEarly) {
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = fmaf((v[j][e] - mean) * rstd, gv[e], bv[e]);
+          for (int e = 0; e < VEC; ++e) o[e] = fmaf((v[j][e] - mean) * rstd, gv[j][e], bv[j][e]);
+        } else {
+          float gl[VEC], bl[VEC];
+          load_param<T, VEC>(g + idx, gl);
+          load_param<T, VEC>(b + idx, bl);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) o[e] = fmaf((v[j][e] - mean) * rstd, gl[e], bl[e]);
+        }
         store_vec<T, VEC>(y + idx, o);
       }
     }

@@ -1,8 +1,9 @@
 """Parity of the GEMM epilogue kernels with the CPU oracle (GPU).
 
 bf16 operands run on the tcgen05 tensor-core kernel (TMA-addressable shapes)
-or the CUDA-core kernel (K not a multiple of 8); fp32 operands run on the
-CUDA-core kernel.  Tolerances: bf16 epilogues rtol 2e-2 / atol 2e-2 against
+or the CUDA-core kernel (K not a multiple of 8); fp32 operands run on the same
+tensor-core kernel through a three-part bf16 split (m*n*k >= 4e6) or on the
+CUDA-core kernel (smaller problems).  Tolerances: bf16 epilogues rtol 2e-2 / atol 2e-2 against
 the fp32-accumulated reference (BASELINE), fp32 epilogues rtol/atol 3e-4
 (reference tests/test_gemm_bias_gelu_v0.py).  Shapes follow the reference's
 tests (tests/test_gemm_swiglu_v4.py:16-28, test_gemm_swiglu_v11.py:19-31)
@@ -119,8 +120,10 @@ def test_gemm_bias_gelu_bf16(m, k, n):
     close(actual, oracle.gemm_bias_gelu(x.float(), w.float(), bias), BF_RTOL, BF_ATOL)
 
 
+# below 4e6 multiply-adds: CUDA cores; from (64, 256, 512) on: tensor cores,
+# including ragged K (77, 520: split parts padded to 64) and ragged M/N
 FP32_SHAPES = [(1, 1, 1), (1, 7, 13), (4, 16, 32), (17, 31, 63), (32, 128, 256), (64, 256, 512),
-               (128, 512, 1024)]
+               (300, 77, 515), (1, 1024, 4096), (257, 520, 1000), (128, 512, 1024)]
 
 
 @pytest.mark.parametrize("version", range(7))
@@ -149,6 +152,24 @@ def test_fp32_gemm_swiglu(version, m, k, n):
         actual = fn(x.to(DEV), torch.cat((wg, wu), 0).to(DEV))
     expected = oracle.gemm_swiglu(x, wg, wu)
     close(actual, expected, F32_TOL, F32_TOL * max(1.0, float(expected.abs().max()) / 100))
+
+
+@pytest.mark.parametrize(("m", "k", "n"), [(256, 2048, 512), (130, 4000, 260)])
+def test_fp32_tensor_core_split_matches_float64(m, k, n):
+    # The three-part split keeps ~24 significand bits per operand and the
+    # chunked accumulation keeps the tensor core's truncating adds short:
+    # against a float64 GEMM the error stays below 3e-7 of sum_k |x||w| (one
+    # unchunked accumulation reaches ~4e-6 at k = 2048, a bf16-only GEMM ~1e-4).
+    g = seeded(20261130 + m + k + n)
+    x = torch.randn(m, k, generator=g) * torch.exp(torch.randn(m, 1, generator=g))
+    w = torch.randn(n, k, generator=g)
+    bias = torch.zeros(n)
+    actual = b.gemm_bias_gelu_v0(x.to(DEV), w.to(DEV), bias.to(DEV)).cpu().double()
+    pre = x.double() @ w.double().T
+    expected = torch.nn.functional.gelu(pre)
+    scale = x.double().abs() @ w.double().abs().T
+    err = (actual - expected).abs() / (scale + 1e-30)
+    assert float(err.max()) < 3e-7, float(err.max())
 
 
 def test_gemm_golden_cases(golden):

@@ -22,7 +22,9 @@ pytestmark = pytest.mark.gpu
 RTOL, ATOL = 1e-5, 1e-6
 SHAPES = [(0, 128), (1, 1), (1, 3), (2, 31), (2, 32), (2, 33), (7, 127), (64, 128), (33, 512),
           (17, 1024), (8, 4097), (11, 257), (32, 4096), (128, 4096), (128, 8192), (5, 12289),
-          (3, 33000), (2, 40000)]
+          (3, 33000), (2, 40000),
+          # cluster path (few rows, 513..4096 vectors): partial, empty and full last CTA
+          (3, 2052), (7, 6144), (100, 16384), (296, 4096)]
 DEV = "cuda"
 
 

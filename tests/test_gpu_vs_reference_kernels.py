@@ -135,7 +135,7 @@ def test_gemm_swiglu_vs_reference_kernels(libs, m, k, n):
     torch.testing.assert_close(o1, o2, rtol=2e-2, atol=2e-2)
 
 
-@pytest.mark.parametrize(("m", "k", "n"), [(17, 31, 63), (128, 512, 1024)])
+@pytest.mark.parametrize(("m", "k", "n"), [(17, 31, 63), (128, 512, 1024), (512, 4096, 4096)])
 def test_fp32_gemm_bias_gelu_vs_reference_kernels(libs, m, k, n):
     g = seeded(m * 3 + k + n)
     x = torch.randn(m, k, generator=g).to(DEV)
@@ -146,5 +146,27 @@ def test_fp32_gemm_bias_gelu_vs_reference_kernels(libs, m, k, n):
         o1, o2 = torch.empty(m, n, device=DEV), torch.empty(m, n, device=DEV)
         run_both(libs, symbol, lambda o: (_p(x), _p(w), _p(bias), _p(o), ctypes.c_uint64(m),
                                           ctypes.c_uint64(k), ctypes.c_uint64(n), _s()),
-                 o1, o2, f"{symbol}[{m}x{k}x{n}]", time_it=False)
+                 o1, o2, f"{symbol}[{m}x{k}x{n}]", time_it=m >= 512)
+        # unit-variance operands: |x.w| ~ sqrt(k); fp32 sums in a different
+        # order differ by ~1e-7 * k relative to that scale
         torch.testing.assert_close(o1, o2, rtol=3e-4, atol=3e-4 * k ** 0.5, msg=symbol)
+
+
+@pytest.mark.parametrize(("m", "k", "n"), [(512, 4096, 4096)])
+def test_fp32_gemm_swiglu_vs_reference_kernels(libs, m, k, n):
+    g = seeded(m * 5 + k + n)
+    x = torch.randn(m, k, generator=g).to(DEV)
+    w = (torch.randn(2 * n, k, generator=g) * k ** -0.5).to(DEV)
+    ws1, ws2 = torch.empty(m, 2 * n, device=DEV), torch.empty(m, 2 * n, device=DEV)
+    o1, o2 = torch.empty(m, n, device=DEV), torch.empty(m, n, device=DEV)
+    ours, ref = libs
+    make = lambda ws: (lambda o: (_p(x), _p(w), _p(ws), _p(o), ctypes.c_uint64(m),  # noqa: E731
+                                  ctypes.c_uint64(k), ctypes.c_uint64(n), _s()))
+    ours.check(ours.handle.cuda_operator_gemm_swiglu_v3(*make(ws1)(o1)))
+    ref.check(ref.handle.cuda_operator_gemm_swiglu_v3(*make(ws2)(o2)))
+    torch.cuda.synchronize()
+    TIMINGS[f"gemm_swiglu_v3_fp32[{m}x{k}x{n}]"] = {
+        "ours_us": round(_time_us(lambda: ours.handle.cuda_operator_gemm_swiglu_v3(*make(ws1)(o1)), 5), 3),
+        "reference_us": round(_time_us(lambda: ref.handle.cuda_operator_gemm_swiglu_v3(*make(ws2)(o2)), 5), 3),
+    }
+    torch.testing.assert_close(o1, o2, rtol=3e-4, atol=3e-4)
