@@ -15,8 +15,9 @@ from pinned host memory and the output shard copied back inside every step),
 ``cpu_baseline`` (the CPU oracle on a row sample, rank 0 at N=1), ``clocks``
 (nvidia-smi sampled during the timed region), ``gpu_launches`` and ``ops``
 (every other BASELINE config: per-op device time, GB/s or TFLOP/s and the
-fraction of the measured peak; the large RMSNorm and the 2^30 reduction are
-measured sharded at every N).
+fraction of the measured peak, timed from CUDA graphs of back-to-back calls --
+cold rotates over input sets three times the L2 size, warm repeats one set;
+the large RMSNorm and the 2^30 reduction are measured sharded at every N).
 
 ``--impl reference`` times the reference's CPU path (the CPU oracle) on a
 bounded row sample of the same workload, on rank 0 only.
@@ -243,11 +244,53 @@ def event_median_us(fn, reps: int, flush=None) -> float:
     return statistics.median(samples)
 
 
+def graph_us(calls, reps: int = 20) -> float:
+    """Device time per call of the closures `calls`, captured once into a CUDA
+    graph and replayed back to back (no host launch cost between calls)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for c in calls[:2]:
+            c()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for c in calls:
+            c()
+    graph.replay()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        graph.replay()
+    end.record()
+    end.synchronize()
+    us = start.elapsed_time(end) * 1000.0 / (reps * len(calls))
+    del graph
+    return us
+
+
+def rotation(make, nbytes: int, min_calls: int = 64) -> tuple[list, list]:
+    """Closures over input sets whose total is 3x the L2 (every call reads
+    cold data, and nothing is flushed inside the timed replay), and the same
+    number of calls on set 0 (warm L2)."""
+    l2 = torch.cuda.get_device_properties(torch.cuda.current_device()).L2_cache_size
+    nsets = max(2, -(-3 * l2 // max(nbytes, 1)))
+    sets = [make(i) for i in range(nsets)]
+    reps = max(min_calls, nsets)
+    cold = [sets[i % nsets] for i in range(reps)]
+    warm = [sets[0]] * reps
+    return cold, warm
+
+
 def op_table(d: Dist, pk: dict) -> dict:
     """Every other BASELINE config at N=1 (rank 0), plus the sharded large
-    RMSNorm and 2^30 reduction at every N.  Cold = L2 flushed before each rep."""
+    RMSNorm and 2^30 reduction at every N.  Single-GPU configs are timed from
+    CUDA graphs of back-to-back calls: cold rotates over input sets 3x the
+    L2 size, warm repeats one set."""
     from cuda_operator_lab import bindings as b
-    from cuda_operator_lab.benchmarking import L2Flusher, measure_batch_us
+    from cuda_operator_lab.benchmarking import L2Flusher
 
     dev = torch.device("cuda")
     ops: dict = {}
@@ -255,17 +298,21 @@ def op_table(d: Dist, pk: dict) -> dict:
     tc = pk["bf16_tflops"]
     flush = L2Flusher(dev)
 
-    def mem_op(name, fn, nbytes, reps=50):
-        warm = measure_batch_us(fn, warmup=3, repeats=reps)
-        cold = event_median_us(fn, reps, flush)
-        ops[name] = {"us_warm": round(warm, 3), "us_cold": round(cold, 3),
+    def mem_op(name, make, nbytes):
+        cold_calls, warm_calls = rotation(make, nbytes)
+        cold = graph_us(cold_calls)
+        warm = graph_us(warm_calls)
+        ops[name] = {"us_cold": round(cold, 3), "us_warm": round(warm, 3),
                      "gbs_cold": round(nbytes / cold / 1e3, 1),
                      "frac_cold": round(nbytes / cold / 1e3 / hbm, 3), "bytes": nbytes}
+        torch.cuda.empty_cache()
 
-    def tc_op(name, fn, flops, reps=30):
-        us = event_median_us(fn, reps, flush)
+    def tc_op(name, make, flops, nbytes):
+        cold_calls, _ = rotation(make, nbytes, min_calls=12)
+        us = graph_us(cold_calls, reps=5)
         ops[name] = {"us_cold": round(us, 3), "tflops": round(flops / us / 1e6, 1),
                      "frac": round(flops / us / 1e6 / tc, 3), "flops": flops}
+        torch.cuda.empty_cache()
 
     g = torch.Generator(device=dev)
     g.manual_seed(SEED + 1)
@@ -303,65 +350,110 @@ def op_table(d: Dist, pk: dict) -> dict:
     def randn(*shape, scale=1.0):
         return torch.randn(*shape, device=dev, generator=g) * scale
 
-    x = randn(128, 8192)
-    w = torch.rand(8192, device=dev, generator=g) + 0.5
-    y = torch.empty_like(x)
-    mem_op("rmsnorm_fp32_128x8192", lambda: b.rmsnorm_v4_into(x, w, y, EPS), 2 * x.numel() * 4 + 8192 * 4)
-    x = randn(128, 4096, scale=2.0)
-    y = torch.empty_like(x)
-    mem_op("softmax_fp32_128x4096", lambda: b.softmax_v5_into(x, y), 2 * x.numel() * 4)
-    gam = torch.rand(4096, device=dev, generator=g) + 0.5
-    bet = randn(4096, scale=0.1)
-    mem_op("layernorm_fp32_128x4096", lambda: b.layernorm_v5_into(x, gam, bet, y),
-           2 * x.numel() * 4 + 2 * 4096 * 4)
-    r = randn(128, 4096)
-    mem_op("residual_layernorm_fp32_128x4096", lambda: b.fused_residual_layernorm_v4_into(
-        x, r, gam, bet, y), 3 * x.numel() * 4 + 2 * 4096 * 4)
-    h = torch.empty_like(x)
-    mem_op("residual_layernorm_h_fp32_128x4096", lambda: b.fused_residual_layernorm_h_into(
-        x, r, gam, bet, h, y), 4 * x.numel() * 4 + 2 * 4096 * 4)
-    xr = torch.rand(16_777_216, device=dev, generator=g) * 2 - 1
-    s = torch.empty(1, device=dev)
-    mem_op("reduction_fp32_16777216", lambda: b.reduction_v5_into(xr, s), xr.numel() * 4)
-    x = randn(1024, 4096)
-    bias = randn(4096, scale=0.1)
-    y = torch.empty_like(x)
-    mem_op("bias_gelu_fp32_1024x4096", lambda: b.fused_bias_gelu_v2_into(x, bias, y),
-           2 * x.numel() * 4 + 4096 * 4)
-    u = randn(1024, 4096)
-    mem_op("swiglu_fp32_1024x4096", lambda: b.swiglu_v2_into(x, u, y), 3 * x.numel() * 4)
+    def rmsnorm_set(i):
+        x = randn(128, 8192)
+        w = torch.rand(8192, device=dev, generator=g) + 0.5
+        y = torch.empty_like(x)
+        return lambda: b.rmsnorm_v4_into(x, w, y, EPS)
 
-    xb = randn(512, 4096).to(torch.bfloat16)
-    wb = randn(8192, 4096, scale=4096 ** -0.5).to(torch.bfloat16)
-    ws32 = torch.empty(512, 8192, device=dev)
-    o32 = torch.empty(512, 4096, device=dev)
-    ob = torch.empty(512, 4096, device=dev, dtype=torch.bfloat16)
+    mem_op("rmsnorm_fp32_128x8192", rmsnorm_set, 2 * 128 * 8192 * 4 + 8192 * 4)
+
+    def softmax_set(i):
+        x = randn(128, 4096, scale=2.0)
+        y = torch.empty_like(x)
+        return lambda: b.softmax_v5_into(x, y)
+
+    mem_op("softmax_fp32_128x4096", softmax_set, 2 * 128 * 4096 * 4)
+
+    def ln_set(kind):
+        def make(i):
+            x, r = randn(128, 4096), randn(128, 4096)
+            gam = torch.rand(4096, device=dev, generator=g) + 0.5
+            bet = randn(4096, scale=0.1)
+            y, h = torch.empty_like(x), torch.empty_like(x)
+            return {"ln": lambda: b.layernorm_v5_into(x, gam, bet, y),
+                    "res": lambda: b.fused_residual_layernorm_v4_into(x, r, gam, bet, y),
+                    "res_h": lambda: b.fused_residual_layernorm_h_into(x, r, gam, bet, h, y)}[kind]
+        return make
+
+    elems = 128 * 4096
+    mem_op("layernorm_fp32_128x4096", ln_set("ln"), 2 * elems * 4 + 2 * 4096 * 4)
+    mem_op("residual_layernorm_fp32_128x4096", ln_set("res"), 3 * elems * 4 + 2 * 4096 * 4)
+    mem_op("residual_layernorm_h_fp32_128x4096", ln_set("res_h"), 4 * elems * 4 + 2 * 4096 * 4)
+
+    def reduction_set(i):
+        xr = torch.rand(16_777_216, device=dev, generator=g) * 2 - 1
+        s = torch.empty(1, device=dev)
+        return lambda: b.reduction_v5_into(xr, s)
+
+    mem_op("reduction_fp32_16777216", reduction_set, 16_777_216 * 4)
+
+    def bias_gelu_set(i):
+        x, bias = randn(1024, 4096), randn(4096, scale=0.1)
+        y = torch.empty_like(x)
+        return lambda: b.fused_bias_gelu_v2_into(x, bias, y)
+
+    mem_op("bias_gelu_fp32_1024x4096", bias_gelu_set, 2 * 1024 * 4096 * 4 + 4096 * 4)
+
+    def swiglu_set(i):
+        x, u = randn(1024, 4096), randn(1024, 4096)
+        y = torch.empty_like(x)
+        return lambda: b.swiglu_v2_into(x, u, y)
+
+    mem_op("swiglu_fp32_1024x4096", swiglu_set, 3 * 1024 * 4096 * 4)
+
     fl = 2 * 512 * 4096 * 8192
-    tc_op("gemm_swiglu_bf16_512x4096x4096_fp32out_v11", lambda: b.gemm_swiglu_v11_into(xb, wb, ws32, o32), fl)
-    tc_op("gemm_swiglu_bf16_512x4096x4096_bf16out", lambda: b.gemm_swiglu_bf16_into(xb, wb, ob), fl)
+    xb = randn(512, 4096).to(torch.bfloat16)
+
+    def swiglu_gemm_set(out_kind):
+        def make(i):
+            wb = randn(8192, 4096, scale=4096 ** -0.5).to(torch.bfloat16)
+            if out_kind == "fp32":
+                ws32 = torch.empty(512, 8192, device=dev)
+                o32 = torch.empty(512, 4096, device=dev)
+                return lambda: b.gemm_swiglu_v11_into(xb, wb, ws32, o32)
+            ob = torch.empty(512, 4096, device=dev, dtype=torch.bfloat16)
+            return lambda: b.gemm_swiglu_bf16_into(xb, wb, ob)
+        return make
+
+    tc_op("gemm_swiglu_bf16_512x4096x4096_fp32out_v11", swiglu_gemm_set("fp32"), fl, 8192 * 4096 * 2)
+    tc_op("gemm_swiglu_bf16_512x4096x4096_bf16out", swiglu_gemm_set("bf16"), fl, 8192 * 4096 * 2)
     xs_ = randn(128, 64).to(torch.bfloat16)
     wsm = randn(4096, 64, scale=0.125).to(torch.bfloat16)
     os_ = torch.empty(128, 2048, device=dev)
     ws_ = torch.empty(128, 4096, device=dev)
-    us = measure_batch_us(lambda: b.gemm_swiglu_v11_into(xs_, wsm, ws_, os_), warmup=5,
-                          repeats=200)
-    us_single = event_median_us(lambda: b.gemm_swiglu_v11_into(xs_, wsm, ws_, os_), 100)
+    small = lambda: b.gemm_swiglu_v11_into(xs_, wsm, ws_, os_)  # noqa: E731
+    us_graph = graph_us([small] * 64)
+    us_single = event_median_us(small, 100)
     ops["gemm_swiglu_bf16_128x64x2048_v11"] = {
-        "us_back_to_back": round(us, 3), "us_single_call": round(us_single, 3),
-        "tflops": round(2 * 128 * 64 * 4096 / us / 1e6, 2)}
-    wg = randn(4096, 4096, scale=4096 ** -0.5).to(torch.bfloat16)
-    bg = randn(4096, scale=0.1)
-    og = torch.empty(512, 4096, device=dev, dtype=torch.bfloat16)
-    tc_op("gemm_bias_gelu_bf16_512x4096x4096", lambda: b.gemm_bias_gelu_bf16_into(xb, wg, bg, og),
-          2 * 512 * 4096 * 4096)
+        "us_back_to_back": round(us_graph, 3), "us_single_call": round(us_single, 3),
+        "tflops": round(2 * 128 * 64 * 4096 / us_graph / 1e6, 2)}
+
+    def gelu_gemm_set(dtype):
+        def make(i):
+            bg = randn(4096, scale=0.1)
+            if dtype == "bf16":
+                wg = randn(4096, 4096, scale=4096 ** -0.5).to(torch.bfloat16)
+                og = torch.empty(512, 4096, device=dev, dtype=torch.bfloat16)
+                return lambda: b.gemm_bias_gelu_bf16_into(xb, wg, bg, og)
+            wf = randn(4096, 4096, scale=4096 ** -0.5)
+            of = torch.empty(512, 4096, device=dev)
+            return lambda: b.gemm_bias_gelu_v0_into(xf, wf, bg, of)
+        return make
+
+    tc_op("gemm_bias_gelu_bf16_512x4096x4096", gelu_gemm_set("bf16"), 2 * 512 * 4096 * 4096,
+          4096 * 4096 * 2)
     xf = randn(512, 4096)
-    wf = randn(4096, 4096, scale=4096 ** -0.5)
-    of = torch.empty(512, 4096, device=dev)
-    tc_op("gemm_bias_gelu_fp32_512x4096x4096_v0", lambda: b.gemm_bias_gelu_v0_into(
-        xf, wf, bg, of), 2 * 512 * 4096 * 4096, reps=20)
-    wf2 = randn(8192, 4096, scale=4096 ** -0.5)
-    tc_op("gemm_swiglu_fp32_512x4096x4096_v3", lambda: b.gemm_swiglu_v3_into(
-        xf, wf2, ws32, o32), fl, reps=20)
+    tc_op("gemm_bias_gelu_fp32_512x4096x4096_v0", gelu_gemm_set("fp32"), 2 * 512 * 4096 * 4096,
+          4096 * 4096 * 4)
+
+    def swiglu_fp32_set(i):
+        wf2 = randn(8192, 4096, scale=4096 ** -0.5)
+        ws = torch.empty(512, 8192, device=dev)
+        o = torch.empty(512, 4096, device=dev)
+        return lambda: b.gemm_swiglu_v3_into(xf, wf2, ws, o)
+
+    tc_op("gemm_swiglu_fp32_512x4096x4096_v3", swiglu_fp32_set, fl, 8192 * 4096 * 4)
     return ops
 
 

@@ -39,6 +39,12 @@ struct DeviceInfo {
 // blocks stay mapped), shared by the operators that need scratch.
 cudaError_t library_pool(cudaMemPool_t* pool);
 
+// Stream-ordered scratch on stream s: from library_pool normally; while s is
+// being captured into a CUDA graph, from cudaMallocAsync (a graph memory
+// node), since creating the pool is not a capturable operation.  Release
+// with cudaFreeAsync on the same stream.
+cudaError_t scratch_alloc(void** ptr, std::size_t bytes, cudaStream_t s);
+
 inline const DeviceInfo& device_info(int* device_out = nullptr) {
   constexpr int kMaxDevices = 64;
   static DeviceInfo infos[kMaxDevices];

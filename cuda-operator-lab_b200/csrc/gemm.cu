@@ -264,10 +264,6 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
     p.b_row_stride = 2 * bnh;
     p.b1_row_offset = bnh;
   }
-  // Few M-blocks per weight tile: the weights stream from DRAM with little L2
-  // reuse, so warm L2 ahead of the ring.  Many M-blocks: the raster already
-  // keeps each weight tile L2-resident across its M-group.
-  p.prefetch_b = (mblocks <= 8 && ops.seg_k_blocks == 0) ? 1 : 0;
   p.out_ld = static_cast<int>(n);
   p.out_vec_ok = col::aligned16(out) && ((n * sizeof(TOut)) % 16 == 0);
   p.flush_k_blocks = FLUSH ? kFlushKBlocks : 0;
@@ -402,10 +398,8 @@ int gemm_fp32_tc(const float* x, const float* w0, const float* w1, BMode mode, c
   const std::uint64_t b_rows = mode == BMode::kSwiGLU ? 2 * n : n;
   const std::size_t a_bytes = static_cast<std::size_t>(m) * 3 * kp * 2;
   const std::size_t b_bytes = static_cast<std::size_t>(b_rows) * 3 * kp * 2;
-  cudaMemPool_t pool = nullptr;
-  if (col::library_pool(&pool) != cudaSuccess) return -1;
   void* scratch = nullptr;
-  if (cudaMallocFromPoolAsync(&scratch, a_bytes + b_bytes, pool, s) != cudaSuccess) {
+  if (col::scratch_alloc(&scratch, a_bytes + b_bytes, s) != cudaSuccess) {
     cudaGetLastError();
     return -1;
   }

@@ -45,7 +45,6 @@ enum Epilogue : int {
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;  // bf16 elements per k-block: one 128-byte swizzle row
 constexpr int kGroupM = 16;  // m-blocks per rasterisation group (L2 reuse of B)
-constexpr int kPrefetchDepth = 8;  // k-blocks between an L2 prefetch and its load
 constexpr int kEpiWarps = 8;       // warps 4..11: two per TMEM lane quarter
 constexpr int kEpiGroups = kEpiWarps / 4;
 constexpr int kCtaThreads = 128 + 32 * kEpiWarps;  // producer, MMA, TMEM, idle + epilogue
@@ -74,7 +73,6 @@ struct __align__(64) GemmParams {
   int b1_row_offset;  // box-1 row relative to box 0
   int out_ld;         // output row stride in elements
   int out_vec_ok;     // 16-byte vector stores allowed
-  int prefetch_b;     // issue L2 prefetches for B boxes ahead of the ring
   // Segmented K (fp32 operands split into bf16 parts, see gemm.cu): when
   // seg_k_blocks > 0 the k-loop runs over num_k_blocks = segments *
   // seg_k_blocks blocks; segment s reads A from part (seg_pairs >> 4s) & 3
@@ -218,6 +216,40 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Epilogue-side wait on an accumulator barrier.  Lane 0 alone polls,
+// sleeping kEpiPollSleepNs between polls, then the warp agrees: the epilogue
+// waits on whole tiles, so waking ~0.1 us late costs nothing, while 256
+// threads polling would take shared-memory and issue slots from the TMA and
+// MMA threads that share their SM sub-partitions.  __syncwarp orders the
+// other lanes after lane 0's acquire.  Same time limit as mbar_wait.
+constexpr unsigned kEpiPollSleepNs = 64;
+
+__device__ __forceinline__ bool epi_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                         int lane) {
+  int got = 0;
+  if (lane == 0) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 1;; ++i) {
+      if (mbar_try_wait(bar, parity)) {
+        got = 1;
+        break;
+      }
+      if (kEpiPollSleepNs) __nanosleep(kEpiPollSleepNs);
+      if ((i & 15u) == 0u) {
+        if (*abort_flag) break;
+        const uint64_t now = globaltimer_ns();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > kWaitLimitNs) {
+          break;
+        }
+      }
+    }
+  }
+  __syncwarp();
+  return __shfl_sync(0xffffffffu, got, 0) != 0;
+}
+
 // Bounded wait that ignores the abort flag (used while draining).
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
@@ -234,15 +266,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
       : "memory");
-}
-
-// Warm L2 with a box that a later stage will load (no shared memory, no
-// completion tracking; a hint the hardware may drop).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
@@ -636,14 +659,6 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
             tma_load_2d(sa, &p.map_a, fb, ax, a_row);
             tma_load_2d(sb, &p.map_b0, fb, kx, b0_row);
             tma_load_2d(sb + BNH * 128, &p.map_b1, fb, kx, b1_row);
-            // Weight boxes kPrefetchDepth k-blocks ahead go to L2 now, so when
-            // the ring reaches them the TMA reads hit L2 instead of waiting on
-            // DRAM (matters when few M-blocks share each weight tile).
-            if (p.prefetch_b && kb + kPrefetchDepth < p.num_k_blocks) {
-              const int px = kx + kPrefetchDepth * kBlockK;
-              tma_prefetch_l2_2d(&p.map_b0, px, b0_row);
-              tma_prefetch_l2_2d(&p.map_b1, px, b1_row);
-            }
             issued_mask |= 1u << stage;
             issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
             if (++stage == kStages) {
@@ -694,7 +709,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
               tc_fence_after();
               const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
               const uint32_t sb = sa + Cfg::kABytes;
-  #pragma unroll
+#pragma unroll
               for (int k = 0; k < kBlockK / 16; ++k) {
                 umma_bf16(d_tmem, sdesc_kmajor_sw128(sa + k * 32), sdesc_kmajor_sw128(sb + k * 32),
                           kIdesc, (kb != kb0 || k != 0) ? 1u : 0u);
@@ -734,10 +749,9 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
       for (int c = 0; c < chunks; ++c, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        // All lanes wait, then agree, so the warp-collective tcgen05.ld below
-        // always runs with the full warp.
-        const bool got = mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag);
-        if (!__all_sync(0xffffffffu, got)) {
+        // The warp agrees on the outcome, so the warp-collective tcgen05.ld
+        // below always runs with the full warp.
+        if (!epi_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag, lane)) {
           if (lane == 0) fail(kStatusEpilogue);
           ok = false;
           break;

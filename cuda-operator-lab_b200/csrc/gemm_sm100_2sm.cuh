@@ -201,9 +201,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
             k_block_coords(p, kb, ax, kx);
             tma_load_2d_pair(sa, &p.map_a, fb, ax, a_row);
             tma_load_2d_pair(sb, map_b, fb, kx, b_row);
-            if (p.prefetch_b && kb + kPrefetchDepth < p.num_k_blocks) {
-              tma_prefetch_l2_2d(map_b, kx + kPrefetchDepth * kBlockK, b_row);
-            }
             issued_mask |= 1u << stage;
             issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
             if (++stage == kStages) {
@@ -258,7 +255,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
               tc_fence_after();
               const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
               const uint32_t sb = sa + Cfg::kABytes;
-  #pragma unroll
+#pragma unroll
               for (int k = 0; k < kBlockK / 16; ++k) {
                 umma_bf16_pair(d_tmem, sdesc_kmajor_sw128(sa + k * 32),
                                sdesc_kmajor_sw128(sb + k * 32), kIdesc,
@@ -297,8 +294,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
       for (int c = 0; c < chunks; ++c, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        const bool got = mbar_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag);
-        if (!__all_sync(0xffffffffu, got)) {
+        if (!epi_wait(smem_u32(tfull_bar + acc), acc_phase, abort_flag, lane)) {
           if (lane == 0) fail(kStatusEpilogue);
           ok = false;
           break;

@@ -1,7 +1,11 @@
 // Pointwise fused ops: bias + exact GELU (fused_bias_gelu.cuh:5-29) and
 // SwiGLU (swiglu.cuh:5-27).  Both are pure HBM streams: 16-byte loads and
-// stores, several independent vectors in flight per thread, and a grid of a
-// few CTAs per SM that strides over the tensor.
+// stores, several independent vectors in flight per thread, and a grid of
+// exactly one resident wave (SM count x CTAs per SM from the occupancy API)
+// with equal work per CTA, so no SM idles in a partial second wave.  Plain
+// (L2-allocating) loads and stores: the output usually feeds the next kernel.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -9,11 +13,30 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;  // independent 16-byte vectors in flight per thread
 
-unsigned grid_for(std::uint64_t work_items, int per_thread) {
-  const std::uint64_t per_cta = static_cast<std::uint64_t>(kThreads) * per_thread;
-  std::uint64_t blocks = (work_items + per_cta - 1) / per_cta;
-  const std::uint64_t cap = static_cast<std::uint64_t>(col::device_info().sm_count) * 8;
-  if (blocks > cap) blocks = cap;
+// CTAs of `kKernel` resident on the whole device (queried once per device
+// and kernel; 8 per SM if the query fails).
+template <auto kKernel>
+std::uint64_t wave_ctas() {
+  constexpr int kMaxDevices = 64;
+  static int cached[kMaxDevices] = {};
+  static std::once_flag flags[kMaxDevices];
+  int dev = 0;
+  const col::DeviceInfo& info = col::device_info(&dev);
+  std::call_once(flags[dev & 63], [dev]() {
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kKernel, kThreads, 0) != cudaSuccess ||
+        blocks <= 0) {
+      cudaGetLastError();
+      blocks = 8;
+    }
+    cached[dev & 63] = blocks;
+  });
+  return static_cast<std::uint64_t>(info.sm_count) * cached[dev & 63];
+}
+
+unsigned grid_for(std::uint64_t work_items, std::uint64_t wave) {
+  std::uint64_t blocks = (work_items + kThreads - 1) / kThreads;
+  if (blocks > wave) blocks = wave;
   if (blocks == 0) blocks = 1;
   return static_cast<unsigned>(blocks);
 }
@@ -33,8 +56,8 @@ swiglu_vec_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
     for (int j = 0; j < kUnroll; ++j) {
       const std::uint64_t idx = i + j * stride;
       if (idx < nvec) {
-        gv[j] = col::ld_stream_f4(g + idx);
-        uv[j] = col::ld_stream_f4(u + idx);
+        gv[j] = g[idx];
+        uv[j] = u[idx];
       }
     }
 #pragma unroll
@@ -46,7 +69,7 @@ swiglu_vec_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
         r.y = col::silu_f(gv[j].y) * uv[j].y;
         r.z = col::silu_f(gv[j].z) * uv[j].z;
         r.w = col::silu_f(gv[j].w) * uv[j].w;
-        col::st_stream_f4(o + idx, r);
+        o[idx] = r;
       }
     }
   }
@@ -67,14 +90,15 @@ int swiglu_launch(const float* g, const float* u, float* o, std::uint64_t n, cud
   if (col::aligned16(g) && col::aligned16(u) && col::aligned16(o)) {
     const std::uint64_t nvec = n / 4;
     if (nvec) {
-      swiglu_vec_kernel<<<grid_for(nvec, kUnroll), kThreads, 0, s>>>(
+      swiglu_vec_kernel<<<grid_for(nvec, wave_ctas<swiglu_vec_kernel>()), kThreads, 0, s>>>(
           reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(u),
           reinterpret_cast<float4*>(o), nvec);
       done = nvec * 4;
     }
   }
   if (done < n) {
-    swiglu_scalar_kernel<<<grid_for(n - done, 1), kThreads, 0, s>>>(g, u, o, done, n);
+    swiglu_scalar_kernel<<<grid_for(n - done, wave_ctas<swiglu_scalar_kernel>()), kThreads, 0, s>>>(
+        g, u, o, done, n);
   }
   return static_cast<int>(cudaGetLastError());
 }
@@ -97,7 +121,7 @@ bias_gelu_vec_kernel(const float4* __restrict__ x, const float4* __restrict__ b,
 #pragma unroll
     for (int j = 0; j < kUnroll; ++j) {
       const std::uint32_t rr = r + j * rstride;
-      if (rr < rows) xv[j] = col::ld_stream_f4(x + static_cast<std::uint64_t>(rr) * vcols + c);
+      if (rr < rows) xv[j] = x[static_cast<std::uint64_t>(rr) * vcols + c];
     }
 #pragma unroll
     for (int j = 0; j < kUnroll; ++j) {
@@ -108,7 +132,7 @@ bias_gelu_vec_kernel(const float4* __restrict__ x, const float4* __restrict__ b,
         v.y = col::gelu_erf_f(xv[j].y + bv.y);
         v.z = col::gelu_erf_f(xv[j].z + bv.z);
         v.w = col::gelu_erf_f(xv[j].w + bv.w);
-        col::st_stream_f4(o + static_cast<std::uint64_t>(rr) * vcols + c, v);
+        o[static_cast<std::uint64_t>(rr) * vcols + c] = v;
       }
     }
   }
@@ -138,18 +162,20 @@ int bias_gelu(const float* x, const float* b, float* o, std::uint64_t rows, std:
       rows <= 0xffffffffull) {
     const std::uint32_t vcols = c / 4;
     const unsigned gx = (vcols + kThreads - 1) / kThreads;
-    // rows per column-block: enough CTAs for ~8 per SM, each visiting >= kUnroll rows
-    const std::uint64_t target = static_cast<std::uint64_t>(col::device_info().sm_count) * 8;
-    std::uint64_t gy = (target + gx - 1) / gx;
-    const std::uint64_t max_gy = (rows + kUnroll - 1) / kUnroll;
-    if (gy > max_gy) gy = max_gy;
-    if (gy > 65535) gy = 65535;
+    // Row slots per column block: as many as one wave holds, then trimmed so
+    // every slot visits the same number of rows (rows_per = ceil(rows / gy)).
+    const std::uint64_t wave = wave_ctas<bias_gelu_vec_kernel>();
+    std::uint64_t gy = wave / gx;
     if (gy == 0) gy = 1;
+    if (gy > 65535) gy = 65535;
+    const std::uint64_t rows_per = (rows + gy - 1) / gy;
+    gy = (rows + rows_per - 1) / rows_per;
     bias_gelu_vec_kernel<<<dim3(gx, static_cast<unsigned>(gy)), kThreads, 0, s>>>(
         reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(b),
         reinterpret_cast<float4*>(o), static_cast<std::uint32_t>(rows), vcols);
   } else {
-    bias_gelu_scalar_kernel<<<grid_for(rows * c, 1), kThreads, 0, s>>>(x, b, o, rows, c);
+    bias_gelu_scalar_kernel<<<grid_for(rows * c, wave_ctas<bias_gelu_scalar_kernel>()), kThreads, 0,
+                              s>>>(x, b, o, rows, c);
   }
   return static_cast<int>(cudaGetLastError());
 }

@@ -48,6 +48,17 @@ cudaError_t library_pool(cudaMemPool_t* pool) {
   return errors[dev];
 }
 
+cudaError_t scratch_alloc(void** ptr, std::size_t bytes, cudaStream_t s) {
+  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(s, &capturing);
+  if (e != cudaSuccess) return e;
+  if (capturing != cudaStreamCaptureStatusNone) return cudaMallocAsync(ptr, bytes, s);
+  cudaMemPool_t pool = nullptr;
+  e = library_pool(&pool);
+  if (e != cudaSuccess) return e;
+  return cudaMallocFromPoolAsync(ptr, bytes, pool, s);
+}
+
 }  // namespace col
 
 namespace {
@@ -194,16 +205,13 @@ int launch_sum(const float* x, void* out, std::uint64_t n, cudaStream_t s, doubl
 }
 
 // Stream-ordered scratch: allocated and freed on the caller's stream, so
-// concurrent calls on different streams never share it.
+// concurrent calls on different streams never share it (col::scratch_alloc).
 template <bool OUT_F64>
 int reduce_with_pool_scratch(const float* x, void* out, std::uint64_t n, cudaStream_t s) {
   const Plan p = plan_for(n);
   const std::size_t bytes = static_cast<std::size_t>(p.ctas) * sizeof(double) + 16;
-  cudaMemPool_t pool = nullptr;
-  cudaError_t st = col::library_pool(&pool);
-  if (st != cudaSuccess) return static_cast<int>(st);
   void* scratch = nullptr;
-  st = cudaMallocFromPoolAsync(&scratch, bytes, pool, s);
+  cudaError_t st = col::scratch_alloc(&scratch, bytes, s);
   if (st != cudaSuccess) return static_cast<int>(st);
   double* partials = static_cast<double*>(scratch);
   unsigned* counter = reinterpret_cast<unsigned*>(partials + p.ctas);
@@ -221,8 +229,9 @@ int reduce_with_pool_scratch(const float* x, void* out, std::uint64_t n, cudaStr
 // ordered, and different streams get different blocks, so the counter is
 // zero whenever a launch starts and a call is a single kernel launch.  The
 // block is created on the first call on a stream (cudaMalloc plus a memset
-// on that stream); a stream that is being captured into a graph, or more
-// than kMaxStreamScratch streams, use the stream-ordered pool path instead.
+// on that stream); a stream that is being captured into a graph, more than
+// kMaxStreamScratch streams, and cudaStreamPerThread (one handle naming a
+// different stream on every host thread) use the stream-ordered pool path.
 constexpr int kMaxStreamScratch = 256;
 
 struct StreamScratch {
@@ -240,7 +249,7 @@ bool stream_scratch(cudaStream_t s, unsigned ctas, double** partials, unsigned**
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   const unsigned capacity = static_cast<unsigned>(col::device_info().sm_count) *
                             static_cast<unsigned>(resident_ctas_per_sm());
-  if (ctas > capacity) return false;
+  if (ctas > capacity || s == cudaStreamPerThread) return false;
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < used; ++i) {
     if (entries[i].device == dev && entries[i].stream == s) {

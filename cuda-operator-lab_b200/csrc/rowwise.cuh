@@ -33,16 +33,20 @@ struct RowArgs {
 };
 
 // ------------------------------------------------------------ vector access
+//
+// Row data use plain (L2-allocating) loads and stores: a norm's input usually
+// comes from the kernel before it and its output feeds the next one, so both
+// are worth keeping in the 126 MB L2 (streaming hints would evict them).
 
 template <typename T, int VEC>
 __device__ __forceinline__ void load_vec(const T* p, float (&v)[VEC]) {
   if constexpr (std::is_same<T, float>::value && VEC == 4) {
-    const float4 q = ld_stream_f4(reinterpret_cast<const float4*>(p));
+    const float4 q = *reinterpret_cast<const float4*>(p);
     v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
   } else if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
-    unpack_bf16x8(ld_stream_u4(reinterpret_cast<const uint4*>(p)), v);
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(p), v);
   } else if constexpr (std::is_same<T, float>::value && VEC == 1) {
-    v[0] = __ldcs(p);
+    v[0] = *p;
   } else {
     static_assert(std::is_same<T, __nv_bfloat16>::value && VEC == 1, "unsupported vector");
     v[0] = __bfloat162float(p[0]);
@@ -73,11 +77,11 @@ __device__ __forceinline__ float load_param1(const T* p) {
 template <typename T, int VEC>
 __device__ __forceinline__ void store_vec(T* p, const float (&v)[VEC]) {
   if constexpr (std::is_same<T, float>::value && VEC == 4) {
-    st_stream_f4(reinterpret_cast<float4*>(p), make_float4(v[0], v[1], v[2], v[3]));
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
   } else if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
-    st_stream_u4(reinterpret_cast<uint4*>(p), pack_bf16x8(v));
+    *reinterpret_cast<uint4*>(p) = pack_bf16x8(v);
   } else if constexpr (std::is_same<T, float>::value && VEC == 1) {
-    __stcs(p, v[0]);
+    p[0] = v[0];
   } else {
     p[0] = __float2bfloat16_rn(v[0]);
   }

@@ -42,9 +42,13 @@ extern "C" {
  * Accumulates in fp64 with a fixed per-CTA partition and a fixed-order final
  * combine, so the result is bit-reproducible run to run (the reference's
  * fp32 atomicAdd combine, reduction.cu:43, is not).  input may be NULL only
- * when n == 0, in which case out[0] = 0.  Uses a stream-ordered scratch
- * allocation (a library-owned cudaMemPool) of 8 bytes per CTA (at most
- * 8 x SM count CTAs). */
+ * when n == 0, in which case out[0] = 0.  Scratch (8 bytes per CTA, one
+ * resident wave of CTAs) is a block the library allocates once per
+ * (device, stream) on the first call on that stream and keeps; while a
+ * stream is being captured, and for cudaStreamPerThread, it is a
+ * stream-ordered allocation from a library-owned cudaMemPool instead.  A
+ * stream handle must not be destroyed and re-created (same value) while
+ * the old stream still has a reduction in flight. */
 int cuda_operator_reduction_v0(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:8  */
 int cuda_operator_reduction_v1(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:14 */
 int cuda_operator_reduction_v2(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:20 */
