@@ -172,6 +172,23 @@ def test_fp32_tensor_core_split_matches_float64(m, k, n):
     assert float(err.max()) < 3e-7, float(err.max())
 
 
+# Few tiles and long K, including ragged K and N: SwiGLU (fp32 out) and
+# bias+GELU (bf16 out) against the oracle, and reproducible bit for bit.
+@pytest.mark.parametrize(("m", "k", "n"), [(128, 2048, 4096), (256, 1024, 1536), (100, 3000, 300),
+                                           (512, 4096, 4096), (384, 8192, 1000)])
+def test_long_k_few_tiles(m, k, n):
+    x, wg, wu = bf16_inputs(m, k, n, 20261203 + m + k + n)
+    packed = torch.cat((wg, wu), dim=0).contiguous()
+    xd, pd = x.to(DEV), packed.to(DEV)
+    expected = oracle.gemm_swiglu_bf16_fp32_reference(x, packed)
+    first = b.gemm_swiglu_v11(xd, pd)
+    close(first, expected, BF_RTOL, BF_ATOL)
+    assert torch.equal(first, b.gemm_swiglu_v11(xd, pd)), "results must be reproducible"
+    bias = torch.randn(n, generator=seeded(m + n)) * 0.1
+    out = b.gemm_bias_gelu_bf16(xd, wg.to(DEV), bias.to(DEV))
+    close(out, oracle.gemm_bias_gelu(x.float(), wg.float(), bias), BF_RTOL, BF_ATOL)
+
+
 def test_gemm_golden_cases(golden):
     seen = 0
     for case in golden:

@@ -9,7 +9,10 @@ the CPU oracle.  Its GEMM versions that call cuBLAS (v4, v10/v11 off the WMMA
 region, bias+GELU v2..v6 through cuBLASLt) run NVIDIA's library kernels.
 
 With COL_REF_TIMING=path set, the device time of both libraries per case is
-written there as JSON (timing is recorded, not asserted).
+written there as JSON (timing is recorded, not asserted): `reps` calls are
+captured into a CUDA graph and replayed, so the figure is device time per call
+without the host's ctypes/launch cost (eager back-to-back timing if a library
+call cannot be captured).
 """
 
 from __future__ import annotations
@@ -52,10 +55,27 @@ def _s() -> ctypes.c_void_p:
 
 
 def _time_us(fn, reps=20) -> float:
+    """fn() takes no arguments and enqueues on torch's current stream."""
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(5):
+            graph.replay()
+        end.record()
+        end.synchronize()
+        del graph
+        return start.elapsed_time(end) * 1000.0 / (5 * reps)
+    except RuntimeError:
+        torch.cuda.synchronize()
     start.record()
     for _ in range(reps):
         fn()
