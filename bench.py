@@ -537,7 +537,7 @@ def run_ours(args, d: Dist) -> dict | None:
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": round(achieved / pk["bf16_tflops_sustained"], 3),
-                     "traffic": traffic, "kernel": "gemm_bf16_tc_kernel (SwiGLU, bf16 out)",
+                     "traffic": traffic, "kernel": "gemm_bf16_tc2_kernel (CTA pair, SwiGLU, bf16 out)",
                      "peak_source": f"{pk['source']} sustained bf16",
                      "gemm_us_per_launch": round(gemm_us, 2)},
         "cpu_baseline": cpu,
