@@ -145,10 +145,17 @@ enum class BMode { kSwiGLU, kGelu };
 
 // Tile width: the B box height BNH (MMA N = 2*BNH; output columns per tile =
 // BNH for SwiGLU, 2*BNH for GELU).  The persistent grid processes tiles in
-// waves of sm_count; a tile's main loop costs ~2*BNH MMA columns per k-block,
-// so the cost of a choice is waves * 2*BNH.  Ties go to the wider tile (fewer
-// epilogues, better MMA efficiency).  Example: M=512, N=4096 SwiGLU gives 128
-// tiles at BNH=128 (one 86 %-full wave) but exactly 148 at BNH=112.
+// waves of the resident CTAs (or pairs).  A k-block of the main loop costs a
+// nearly width-independent floor -- measured 0.35 us at MMA N = 128 and 0.38 us
+// at N = 256 per CTA pair, the producer/MMA handshake of the pipeline, not
+// the MMA itself -- so a choice costs waves * (kKBlockFloor + 2*BNH), the
+// floor expressed in MMA columns (fitted to those two points).  Fewer waves
+// win; among equal waves the narrower tile wins slightly.  Examples: the
+// N-sharded headline (M=16384, N=7168 per GPU) runs BNH=128 (49 waves) rather
+// than BNH=96 (65 waves, which a pure MMA-column model would pick); M=512,
+// N=4096 SwiGLU runs BNH=112 (74 tiles, one wave).
+constexpr std::uint64_t kKBlockFloor = 1365;
+
 int choose_bnh(int mblocks, std::uint64_t n, bool swiglu, int sm_count, int max_bnh,
                bool with112) {
   constexpr int kCandidates[] = {128, 112, 96, 64};
@@ -159,7 +166,7 @@ int choose_bnh(int mblocks, std::uint64_t n, bool swiglu, int sm_count, int max_
     const std::uint64_t cols = swiglu ? bnh : 2 * bnh;
     const std::uint64_t tiles = static_cast<std::uint64_t>(mblocks) * ((n + cols - 1) / cols);
     const std::uint64_t waves = (tiles + sm_count - 1) / sm_count;
-    const std::uint64_t cost = waves * 2 * bnh;
+    const std::uint64_t cost = waves * (kKBlockFloor + 2 * bnh);
     if (cost < best_cost) {
       best_cost = cost;
       best = bnh;
