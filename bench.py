@@ -402,6 +402,14 @@ def op_table(d: Dist, pk: dict) -> dict:
 
     mem_op("swiglu_fp32_1024x4096", swiglu_set, 3 * 1024 * 4096 * 4)
 
+    def residual_rmsnorm_set(i):
+        x, r = randn(M, K).to(torch.bfloat16), randn(M, K).to(torch.bfloat16)
+        w = (torch.rand(K, device=dev, generator=g) + 0.5).to(torch.bfloat16)
+        h, y = torch.empty_like(x), torch.empty_like(x)
+        return lambda: b.fused_residual_rmsnorm_into(x, r, w, h, y, EPS)
+
+    mem_op("residual_rmsnorm_bf16_16384x4096", residual_rmsnorm_set, 4 * M * K * 2 + K * 2)
+
     fl = 2 * 512 * 4096 * 8192
     xb = randn(512, 4096).to(torch.bfloat16)
 
@@ -446,6 +454,16 @@ def op_table(d: Dist, pk: dict) -> dict:
     xf = randn(512, 4096)
     tc_op("gemm_bias_gelu_fp32_512x4096x4096_v0", gelu_gemm_set("fp32"), 2 * 512 * 4096 * 4096,
           4096 * 4096 * 4)
+
+    def down_proj_set(i):
+        xd = randn(512, 14336).to(torch.bfloat16)
+        wd = randn(4096, 14336, scale=14336 ** -0.5).to(torch.bfloat16)
+        hd = randn(512, 4096).to(torch.bfloat16)
+        od = torch.empty_like(hd)
+        return lambda: b.gemm_residual_bf16_into(xd, wd, hd, od)
+
+    tc_op("gemm_residual_bf16_512x14336x4096", down_proj_set, 2 * 512 * 14336 * 4096,
+          4096 * 14336 * 2)
 
     def swiglu_fp32_set(i):
         wf2 = randn(8192, 4096, scale=4096 ** -0.5)
@@ -625,7 +643,8 @@ def run_reference(args) -> dict:
 
 KERNEL_CASES = ("gemm_swiglu_bf16", "gemm_bias_gelu_bf16", "rmsnorm_bf16", "reduction",
                 "rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "bias_gelu_fp32", "swiglu_fp32",
-                "gemm_bias_gelu_fp32", "gemm_swiglu_fp32")
+                "gemm_bias_gelu_fp32", "gemm_swiglu_fp32", "residual_rmsnorm_bf16",
+                "gemm_residual_bf16")
 
 
 def run_kernel_case(spec: str, reps: int, timed: bool = False) -> None:
@@ -661,6 +680,17 @@ def run_kernel_case(spec: str, reps: int, timed: bool = False) -> None:
         x, w = rn(m, k), rn(2 * n, k) * k ** -0.5
         ws, out = torch.empty(m, 2 * n, device=dev), torch.empty(m, n, device=dev)
         fn = lambda: b.gemm_swiglu_v3_into(x, w, ws, out)  # noqa: E731
+    elif name == "residual_rmsnorm_bf16":
+        r, c = d or (M, K)
+        x, res = rn(r, c).bfloat16(), rn(r, c).bfloat16()
+        w = (torch.rand(c, device=dev, generator=g) + 0.5).bfloat16()
+        h, y = torch.empty_like(x), torch.empty_like(x)
+        fn = lambda: b.fused_residual_rmsnorm_into(x, res, w, h, y, EPS)  # noqa: E731
+    elif name == "gemm_residual_bf16":
+        m, k, n = d or (512, 14336, 4096)
+        x, w = rn(m, k).bfloat16(), (rn(n, k) * k ** -0.5).bfloat16()
+        res, out = rn(m, n).bfloat16(), torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        fn = lambda: b.gemm_residual_bf16_into(x, w, res, out)  # noqa: E731
     elif name == "rmsnorm_bf16":
         r, c = d or (M, K)
         x, w = rn(r, c).bfloat16(), (torch.rand(c, device=dev, generator=g) + 0.5).bfloat16()

@@ -222,7 +222,8 @@ bool flush_wide_ok(bool pair) {
 
 template <int EPI, typename TOut, bool FLUSH = false>
 int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, void* out,
-                       std::uint64_t m, std::uint64_t n, cudaStream_t s) {
+                       std::uint64_t m, std::uint64_t n, cudaStream_t s,
+                       const void* residual = nullptr) {
   int dev = 0;
   const col::DeviceInfo& info = col::device_info(&dev);
   if (info.cc_major != 10) return col::kErrDeviceNotSupported;
@@ -253,6 +254,7 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
   if (rc == col::kErrTensorMapEncode) return -1;  // layout TMA cannot express: CUDA cores
   if (rc != 0) return rc;
   p.bias = bias;
+  p.residual = residual;
   p.out = out;
   p.status = status;
   p.m = static_cast<int>(m);
@@ -320,14 +322,15 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
 // bf16 operands straight from the caller: x [m, k], w0/w1 [n, k] (kGelu: w0 only).
 template <int EPI, typename TOut>
 int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, const float* bias,
-                 void* out, std::uint64_t m, std::uint64_t n, std::uint64_t k, cudaStream_t s) {
+                 void* out, std::uint64_t m, std::uint64_t n, std::uint64_t k, cudaStream_t s,
+                 const void* residual = nullptr) {
   if ((k % 8) != 0 || !col::aligned16(x) || !col::aligned16(w0) ||
       (mode == BMode::kSwiGLU && !col::aligned16(w1))) {
     return -1;
   }
   TcOperands ops{x, k, w0, mode == BMode::kSwiGLU ? w1 : w0, n, k,
                  static_cast<int>((k + col::sm100::kBlockK - 1) / col::sm100::kBlockK), 0, 0u};
-  return launch_tensor_gemm<EPI, TOut>(ops, mode, bias, out, m, n, s);
+  return launch_tensor_gemm<EPI, TOut>(ops, mode, bias, out, m, n, s, residual);
 }
 
 // ---------------------------------------------------------------- fp32 on tensor cores
@@ -428,8 +431,9 @@ int gemm_fp32_tc(const float* x, const float* w0, const float* w1, BMode mode, c
 
 template <typename TIn, int EPI, typename TOut>
 int gemm_simt(const void* x, const void* w0, const void* w1, const float* bias, void* out,
-              std::uint64_t m, std::uint64_t n, std::uint64_t k, cudaStream_t s) {
-  col::simt::SimtParams p{x, w0, w1, bias, out, static_cast<int>(m), static_cast<int>(n),
+              std::uint64_t m, std::uint64_t n, std::uint64_t k, cudaStream_t s,
+              const void* residual = nullptr) {
+  col::simt::SimtParams p{x, w0, w1, bias, residual, out, static_cast<int>(m), static_cast<int>(n),
                           static_cast<int>(k)};
   return col::simt::launch_simt<TIn, EPI, TOut>(p, s);
 }
@@ -641,6 +645,36 @@ COL_API int cuda_operator_gemm_bias_gelu_bf16(const void* input_bf16, const void
   if (rc != -1) return rc;
   return gemm_simt<__nv_bfloat16, col::sm100::kEpiBiasGeluErf, __nv_bfloat16>(
       input_bf16, weight_bf16, nullptr, bias, output_bf16, m, n, k, s);
+}
+
+// Down projection with the residual add fused (no reference counterpart):
+// out[m, n] = bf16(x[m, :] . w[n, :] + residual[m, n]), fp32 accumulation,
+// bf16 x [M, K], W [N, K], residual and out [M, N].  out may be the residual
+// buffer itself (each element is read before it is written, by the same
+// thread).  m == 0 or n == 0 succeeds first; NULL, k == 0 or sizes above
+// INT32_MAX are invalid.
+COL_API int cuda_operator_gemm_residual_bf16(const void* input_bf16, const void* weight_bf16,
+                                             const void* residual_bf16, void* output_bf16,
+                                             uint64_t m, uint64_t k, uint64_t n, void* stream) {
+  if (m == 0 || n == 0) return 0;
+  if (!input_bf16 || !weight_bf16 || !residual_bf16 || !output_bf16 ||
+      !dims_ok(m, n, k, 0x7fffffffull)) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  const cudaStream_t s = col::as_stream(stream);
+  // The vector residual loads share the output's alignment test.
+  const bool same_alignment =
+      (reinterpret_cast<std::uintptr_t>(residual_bf16) & 15u) ==
+      (reinterpret_cast<std::uintptr_t>(output_bf16) & 15u);
+  int rc = -1;
+  if (same_alignment) {
+    rc = gemm_bf16_tc<col::sm100::kEpiResidual, __nv_bfloat16>(
+        input_bf16, weight_bf16, nullptr, BMode::kGelu, nullptr, output_bf16, m, n, k, s,
+        residual_bf16);
+  }
+  if (rc != -1) return rc;
+  return gemm_simt<__nv_bfloat16, col::sm100::kEpiResidual, __nv_bfloat16>(
+      input_bf16, weight_bf16, nullptr, nullptr, output_bf16, m, n, k, s, residual_bf16);
 }
 
 COL_API int cuda_operator_lab_gemm_status(unsigned int* status, int clear) {

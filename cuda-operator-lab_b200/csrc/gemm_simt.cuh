@@ -30,6 +30,7 @@ struct SimtParams {
   const void* b0;   // gate / W rows [N, K]
   const void* b1;   // up rows [N, K] (SwiGLU only)
   const float* bias;
+  const void* residual;  // kEpiResidual: bf16 [M, N]
   void* out;        // [M, N]
   int m;
   int n;
@@ -117,6 +118,9 @@ __global__ void __launch_bounds__(kThreads) simt_gemm_kernel(const SimtParams p)
         o = silu_f(accg[i][j]) * accu[i][j];
       } else if constexpr (EPI == sm100::kEpiSwiGLURoundBf16) {
         o = silu_f(bf16_round(accg[i][j])) * bf16_round(accu[i][j]);
+      } else if constexpr (EPI == sm100::kEpiResidual) {
+        o = accg[i][j] + __bfloat162float(static_cast<const __nv_bfloat16*>(
+                             p.residual)[static_cast<std::size_t>(gm) * p.n + gn]);
       } else if constexpr (EPI == sm100::kEpiBiasGeluErf) {
         o = gelu_erf_f(accg[i][j] + __ldg(p.bias + gn));
       } else {

@@ -40,6 +40,7 @@ enum Epilogue : int {
   kEpiSwiGLURoundBf16 = 1,  // g, u rounded to bf16 first (bf16 GEMM workspace semantics)
   kEpiBiasGeluErf = 2,      // out = gelu_erf(acc + bias[n])
   kEpiBiasGeluTanh = 3,     // out = gelu_tanh(acc + bias[n])
+  kEpiResidual = 4,         // out = acc + residual[m, n] (bf16 residual, down projection)
 };
 
 constexpr int kBlockM = 128;
@@ -61,6 +62,7 @@ struct __align__(64) GemmParams {
   CUtensorMap map_b0;  // gate rows (SwiGLU) or W rows (GELU)
   CUtensorMap map_b1;  // up rows (SwiGLU) or W rows (GELU)
   const float* bias;
+  const void* residual;  // kEpiResidual: bf16 [m, n], row stride out_ld (may equal out)
   void* out;
   unsigned* status;
   int m;
@@ -455,6 +457,33 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, int row, int co
 
 // ------------------------------------------------------------ epilogue
 
+// 16 residual values (bf16) of row `row` from column col0, zero outside the
+// matrix; two 16-byte loads when the row is fully in range and aligned (the
+// same condition as the vector output store).
+__device__ __forceinline__ void load_residual16(const GemmParams& p, int row, int col0,
+                                                float (&r)[16]) {
+  if (row >= p.m) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) r[j] = 0.0f;
+    return;
+  }
+  const __nv_bfloat16* src =
+      static_cast<const __nv_bfloat16*>(p.residual) + static_cast<std::size_t>(row) * p.out_ld + col0;
+  if (p.out_vec_ok && col0 + 16 <= p.n) {
+    float lo[8], hi[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(src), lo);
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(src + 8), hi);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      r[j] = lo[j];
+      r[8 + j] = hi[j];
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) r[j] = col0 + j < p.n ? __bfloat162float(src[j]) : 0.0f;
+  }
+}
+
 // One accumulator tile, this thread's TMEM lane (one output row): 16-column
 // chunks dealt round-robin to the kEpiGroups warps that share the lane
 // quarter.  SwiGLU: gate at accumulator column c, up at BNH + c, output
@@ -479,6 +508,19 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int row, int 
         }
         o[j] = silu_fast(gv) * uv;
       }
+      store_chunk<TOut, 16>(p, row, col_base + c, o);
+    }
+  } else if constexpr (EPI == kEpiResidual) {
+    const int col_base = nb * 2 * BNH;
+#pragma unroll 1
+    for (int c = group * 16; c < 2 * BNH; c += 16 * kEpiGroups) {
+      uint32_t a[16];
+      tmem_ld16(t_row + c, a);
+      float res[16];
+      load_residual16(p, row, col_base + c, res);
+      float o[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = __uint_as_float(a[j]) + res[j];
       store_chunk<TOut, 16>(p, row, col_base + c, o);
     }
   } else {

@@ -51,3 +51,41 @@ COL_API int cuda_operator_rmsnorm_bf16(const void* input_bf16, const void* weigh
                  static_cast<std::uint32_t>(cols), eps};
   return col::launch_rows<col::RowOp::kRms, __nv_bfloat16, false>(a, col::as_stream(stream));
 }
+
+// Residual add + RMSNorm in one pass (no reference counterpart; the decode /
+// prefill norm that feeds the MLP GEMM): h = input + residual is stored and
+// y = rmsnorm(h) * weight, each input read once.  bf16: h is rounded to bf16
+// before the statistics, exactly as a separate add kernel would leave it.
+// Same argument rules as the RMSNorm entries (rows == 0 succeeds first).
+namespace {
+
+template <typename T>
+int residual_rmsnorm(const void* x, const void* r, const void* w, void* h, void* y,
+                     std::uint64_t rows, std::uint64_t cols, float eps, void* stream) {
+  if (rows == 0) return 0;
+  if (x == nullptr || r == nullptr || w == nullptr || h == nullptr || y == nullptr ||
+      !col::row_dims_ok(rows, cols)) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  if (!(eps > 0.0f)) return static_cast<int>(cudaErrorInvalidValue);
+  col::RowArgs a{x, r, w, nullptr, y, h, rows, static_cast<std::uint32_t>(cols), eps};
+  return col::launch_rows<col::RowOp::kResidualRms, T, true>(a, col::as_stream(stream));
+}
+
+}  // namespace
+
+COL_API int cuda_operator_fused_residual_rmsnorm_bf16(const void* input_bf16,
+                                                      const void* residual_bf16,
+                                                      const void* weight_bf16, void* h_out_bf16,
+                                                      void* output_bf16, uint64_t rows,
+                                                      uint64_t cols, float eps, void* stream) {
+  return residual_rmsnorm<__nv_bfloat16>(input_bf16, residual_bf16, weight_bf16, h_out_bf16,
+                                         output_bf16, rows, cols, eps, stream);
+}
+
+COL_API int cuda_operator_fused_residual_rmsnorm_h(const float* input, const float* residual,
+                                                   const float* weight, float* h_out,
+                                                   float* output, uint64_t rows, uint64_t cols,
+                                                   float eps, void* stream) {
+  return residual_rmsnorm<float>(input, residual, weight, h_out, output, rows, cols, eps, stream);
+}

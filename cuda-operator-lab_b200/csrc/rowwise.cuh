@@ -1,4 +1,5 @@
-// Row engine shared by RMSNorm, LayerNorm, residual+LayerNorm and softmax.
+// Row engine shared by RMSNorm, LayerNorm, residual+LayerNorm, residual+RMSNorm
+// and softmax.
 //
 // One group of TPR threads owns one row.  Each thread loads NV vectors of VEC
 // elements (16-byte vectors when the row width and all pointers allow it,
@@ -18,11 +19,22 @@
 
 namespace col {
 
-enum class RowOp : int { kRms = 0, kLayerNorm = 1, kResidualLayerNorm = 2, kSoftmax = 3 };
+enum class RowOp : int {
+  kRms = 0,
+  kLayerNorm = 1,
+  kResidualLayerNorm = 2,
+  kSoftmax = 3,
+  kResidualRms = 4,
+};
+
+// Ops that normalise h = x + residual (and may store h).
+constexpr bool has_residual(RowOp op) {
+  return op == RowOp::kResidualLayerNorm || op == RowOp::kResidualRms;
+}
 
 struct RowArgs {
   const void* x;
-  const void* residual;  // kResidualLayerNorm only
+  const void* residual;  // residual ops only
   const void* weight;    // RMSNorm weight / LayerNorm gamma
   const void* bias;      // LayerNorm beta
   void* y;
@@ -162,7 +174,9 @@ row_kernel(const RowArgs a) {
       for (int e = 0; e < VEC; ++e) v[j][e] = 0.0f;
     }
   }
-  if constexpr (OP == RowOp::kResidualLayerNorm) {
+  if constexpr (has_residual(OP)) {
+    // h = x + residual in T: for bf16, h is rounded to bf16 before the
+    // statistics, as a separate add kernel writing h would leave it.
     const T* __restrict__ r = static_cast<const T*>(a.residual) + base;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
@@ -170,7 +184,10 @@ row_kernel(const RowArgs a) {
         float rv[VEC];
         load_vec<T, VEC>(r + (static_cast<std::uint32_t>(j) * TPR + t) * VEC, rv);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) v[j][e] += rv[e];
+        for (int e = 0; e < VEC; ++e) {
+          v[j][e] += rv[e];
+          if constexpr (!std::is_same<T, float>::value) v[j][e] = bf16_round(v[j][e]);
+        }
       }
     }
     if constexpr (STORE_H) {
@@ -185,7 +202,7 @@ row_kernel(const RowArgs a) {
   T* __restrict__ y = static_cast<T*>(a.y) + base;
   const float inv_cols = 1.0f / static_cast<float>(cols);
 
-  if constexpr (OP == RowOp::kRms) {
+  if constexpr (OP == RowOp::kRms || OP == RowOp::kResidualRms) {
     // Weights are loaded before the reduction so their latency overlaps it
     // (when the registers allow: up to 16 elements per thread).
     constexpr bool kEarly = NV * VEC <= 16;
@@ -373,18 +390,27 @@ __global__ void __launch_bounds__(kLongThreads) row_kernel_long(const RowArgs a)
   const float inv_cols = 1.0f / static_cast<float>(cols);
 
   auto in = [&](std::uint32_t i) -> float {
-    if constexpr (OP == RowOp::kResidualLayerNorm) return ld1(x + i) + ld1(r + i);
-    else return ld1(x + i);
+    if constexpr (has_residual(OP)) {
+      const float hv = ld1(x + i) + ld1(r + i);
+      if constexpr (std::is_same<T, float>::value) return hv;
+      else return bf16_round(hv);
+    } else {
+      return ld1(x + i);
+    }
   };
 
-  if constexpr (OP == RowOp::kRms) {
+  if constexpr (OP == RowOp::kRms || OP == RowOp::kResidualRms) {
     float s = 0.0f;
     for (std::uint32_t i = threadIdx.x; i < cols; i += kLongThreads) {
       const float v = in(i);
       s = fmaf(v, v, s);
     }
     const float rstd = rsqrtf(block_sum_long(s, sh) * inv_cols + a.eps);
-    for (std::uint32_t i = threadIdx.x; i < cols; i += kLongThreads) st1(y + i, (in(i) * rstd) * ld1(w + i));
+    for (std::uint32_t i = threadIdx.x; i < cols; i += kLongThreads) {
+      const float hv = in(i);
+      if constexpr (STORE_H && OP == RowOp::kResidualRms) st1(static_cast<T*>(a.h) + base + i, hv);
+      st1(y + i, (hv * rstd) * ld1(w + i));
+    }
   } else if constexpr (OP == RowOp::kLayerNorm || OP == RowOp::kResidualLayerNorm) {
     const float shift = in(0);  // shifted sum, as in row_kernel
     float s = 0.0f;
@@ -445,7 +471,7 @@ inline int launch_rows(const RowArgs& a, cudaStream_t s) {
   constexpr int kVec = std::is_same<T, float>::value ? 4 : 8;
   bool vec = (a.cols % kVec) == 0 && aligned16(a.x) && aligned16(a.y) && aligned16(a.weight);
   if (OP == RowOp::kLayerNorm || OP == RowOp::kResidualLayerNorm) vec = vec && aligned16(a.bias);
-  if (OP == RowOp::kResidualLayerNorm) vec = vec && aligned16(a.residual);
+  if (has_residual(OP)) vec = vec && aligned16(a.residual);
   if (STORE_H) vec = vec && aligned16(a.h);
   if (OP == RowOp::kSoftmax) vec = (a.cols % kVec) == 0 && aligned16(a.x) && aligned16(a.y);
   if (vec) return dispatch_row_width<OP, T, kVec, STORE_H>(a.cols / kVec, a, s);

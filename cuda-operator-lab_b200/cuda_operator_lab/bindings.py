@@ -14,9 +14,9 @@ There is no fallback: if the shared library is missing, the first call raises
 ``RuntimeError``.  ``CUDA_OPERATOR_LIB`` overrides the library path
 (reference ``bindings.py:17-21``).
 
-Functions after the reference set (``rmsnorm_bf16``,
-``fused_residual_layernorm_h``, ``gemm_swiglu_bf16``, ``gemm_bias_gelu_bf16``,
-``reduction_partial_f64``) expose the library's additional entry points.
+Functions after the reference set (``rmsnorm_bf16``, ``fused_residual_layernorm_h``,
+``fused_residual_rmsnorm``, ``gemm_swiglu_bf16``, ``gemm_bias_gelu_bf16``,
+``gemm_residual_bf16``, ``reduction_partial_f64``) expose the library's additional entry points.
 """
 
 from __future__ import annotations
@@ -65,8 +65,12 @@ _SIGNATURES["cuda_operator_error_string"] = [_I32]
 _SIGNATURES["cuda_operator_rmsnorm_bf16"] = [_P, _P, _P, _U64, _U64, _F32, _P]
 _SIGNATURES["cuda_operator_fused_residual_layernorm_h"] = [
     _P, _P, _P, _P, _P, _P, _U64, _U64, _F32, _P]
+_SIGNATURES["cuda_operator_fused_residual_rmsnorm_bf16"] = [
+    _P, _P, _P, _P, _P, _U64, _U64, _F32, _P]
+_SIGNATURES["cuda_operator_fused_residual_rmsnorm_h"] = [_P, _P, _P, _P, _P, _U64, _U64, _F32, _P]
 _SIGNATURES["cuda_operator_gemm_swiglu_bf16"] = [_P, _P, _P, _U64, _U64, _U64, _P]
 _SIGNATURES["cuda_operator_gemm_bias_gelu_bf16"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
+_SIGNATURES["cuda_operator_gemm_residual_bf16"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
 _SIGNATURES["cuda_operator_reduction_partial_f64"] = [_P, _P, _U64, _P]
 _SIGNATURES["cuda_operator_lab_device_info"] = [_P, _P, _P]
 _SIGNATURES["cuda_operator_lab_build_tag"] = []
@@ -351,6 +355,41 @@ def rmsnorm_bf16(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5) -> to
 
 
 __all__ += ["rmsnorm_bf16_into", "rmsnorm_bf16"]
+
+
+def fused_residual_rmsnorm_into(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                                h_out: torch.Tensor, out: torch.Tensor,
+                                eps: float = 1e-5) -> tuple[torch.Tensor, torch.Tensor]:
+    """Residual add + RMSNorm in one pass: h_out = x + residual, out = rmsnorm(h) * weight.
+
+    float32 or bfloat16 (all tensors the same dtype); for bfloat16, h is rounded
+    to bfloat16 before the statistics, as a separate add would store it.
+    """
+    dtype = x.dtype if x.dtype in (torch.float32, torch.bfloat16) else torch.float32
+    _validate_rmsnorm_input(x, weight, eps, dtype)
+    if not residual.is_cuda or residual.shape != x.shape or residual.dtype != x.dtype \
+            or not residual.is_contiguous():
+        raise ValueError("rmsnorm residual must be a contiguous CUDA tensor shaped like the input")
+    _validate_rmsnorm_output(x, out)
+    _validate_rmsnorm_output(x, h_out)
+    rows, cols = x.shape
+    if rows == 0:
+        return h_out, out
+    symbol = ("cuda_operator_fused_residual_rmsnorm_bf16" if dtype == torch.bfloat16
+              else "cuda_operator_fused_residual_rmsnorm_h")
+    _call(symbol, _ptr(x), _ptr(residual), _ptr(weight), _ptr(h_out), _ptr(out),
+          ctypes.c_uint64(rows), ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x))
+    return h_out, out
+
+
+def fused_residual_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                           eps: float = 1e-5) -> tuple[torch.Tensor, torch.Tensor]:
+    """Allocating form of :func:`fused_residual_rmsnorm_into`; returns (h, y)."""
+    return fused_residual_rmsnorm_into(x, residual, weight, torch.empty_like(x),
+                                       torch.empty_like(x), eps)
+
+
+__all__ += ["fused_residual_rmsnorm_into", "fused_residual_rmsnorm"]
 
 # ---------------------------------------------------------------- LayerNorm
 # reference bindings.py:875-1151
@@ -657,6 +696,50 @@ def gemm_bias_gelu_bf16(x_bf16: torch.Tensor, weight_bf16: torch.Tensor,
 
 
 __all__ += ["gemm_bias_gelu_bf16_into", "gemm_bias_gelu_bf16"]
+
+
+def gemm_residual_bf16_into(x_bf16: torch.Tensor, weight_bf16: torch.Tensor,
+                            residual_bf16: torch.Tensor, out_bf16: torch.Tensor) -> torch.Tensor:
+    """Down projection with the residual add fused: out = bf16(x @ W.T + residual).
+
+    bf16 x [M, K], W [N, K], residual and out [M, N]; fp32 accumulation.
+    ``out_bf16`` may be ``residual_bf16`` itself (in-place residual update).
+    """
+    tensors = (x_bf16, weight_bf16, residual_bf16, out_bf16)
+    if not all(t.is_cuda for t in tensors):
+        raise ValueError("GEMM residual tensors must be CUDA tensors")
+    if x_bf16.ndim != 2 or weight_bf16.ndim != 2:
+        raise ValueError("x and weight must be 2-D")
+    if x_bf16.shape[1] != weight_bf16.shape[1]:
+        raise ValueError("x.shape[1] must equal weight.shape[1]")
+    expected_shape = (x_bf16.shape[0], weight_bf16.shape[0])
+    if residual_bf16.shape != expected_shape or out_bf16.shape != expected_shape:
+        raise ValueError(f"residual and output shape must be {expected_shape}")
+    if any(t.dtype != torch.bfloat16 for t in tensors):
+        raise TypeError("GEMM residual bf16 expects bfloat16 tensors")
+    if not all(t.is_contiguous() for t in tensors):
+        raise ValueError("all GEMM residual tensors must be contiguous")
+    m, k = x_bf16.shape
+    n = weight_bf16.shape[0]
+    if m == 0 or n == 0:
+        return out_bf16
+    if k == 0:
+        raise ValueError("GEMM residual requires k > 0")
+    _call("cuda_operator_gemm_residual_bf16", _ptr(x_bf16), _ptr(weight_bf16),
+          _ptr(residual_bf16), _ptr(out_bf16), ctypes.c_uint64(m), ctypes.c_uint64(k),
+          ctypes.c_uint64(n), _stream(x_bf16))
+    return out_bf16
+
+
+def gemm_residual_bf16(x_bf16: torch.Tensor, weight_bf16: torch.Tensor,
+                       residual_bf16: torch.Tensor) -> torch.Tensor:
+    """Allocating form of :func:`gemm_residual_bf16_into`."""
+    out = torch.empty((x_bf16.shape[0], weight_bf16.shape[0]), device=x_bf16.device,
+                      dtype=torch.bfloat16)
+    return gemm_residual_bf16_into(x_bf16, weight_bf16, residual_bf16, out)
+
+
+__all__ += ["gemm_residual_bf16_into", "gemm_residual_bf16"]
 
 # ---------------------------------------------------------------- GEMM + SwiGLU
 # reference bindings.py:2036-2818

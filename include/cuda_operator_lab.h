@@ -153,6 +153,17 @@ int cuda_operator_rmsnorm_bf16(const void* input_bf16, const void* weight_bf16, 
  * LayerNorm(h); a transformer block also needs h for its next residual. */
 int cuda_operator_fused_residual_layernorm_h(const float* input, const float* residual, const float* weight, const float* bias, float* h_output, float* output, uint64_t rows, uint64_t cols, float eps, void* stream);
 
+/* Residual add + RMSNorm in one pass: h = input + residual is stored to h_out
+ * and y = (h * rsqrt(mean(h^2) + eps)) * weight to output; every input byte is
+ * read once.  No reference counterpart (its residual fusion exists only for
+ * LayerNorm, fused_residual_layernorm.cuh:5); this is the norm that feeds the
+ * MLP GEMM in a decoder block.  _bf16: bf16 tensors, fp32 statistics, h rounded
+ * to bf16 before the statistics (what a separate add kernel would store);
+ * _h: fp32.  rows == 0 succeeds; NULL, cols == 0 or eps <= 0 return
+ * cudaErrorInvalidValue. */
+int cuda_operator_fused_residual_rmsnorm_bf16(const void* input_bf16, const void* residual_bf16, const void* weight_bf16, void* h_out_bf16, void* output_bf16, uint64_t rows, uint64_t cols, float eps, void* stream);
+int cuda_operator_fused_residual_rmsnorm_h(const float* input, const float* residual, const float* weight, float* h_out, float* output, uint64_t rows, uint64_t cols, float eps, void* stream);
+
 /* Packed GEMM + SwiGLU with bf16 output: out[m, j] = bf16(silu(g) * u), g and u
  * accumulated in fp32 from bf16 x[M, K] and packed W[2N, K].  Same arithmetic
  * as cuda_operator_gemm_swiglu_v4 up to the final rounding; no workspace. */
@@ -162,6 +173,14 @@ int cuda_operator_gemm_swiglu_bf16(const void* input_bf16, const void* packed_we
  * bf16 output, fp32 accumulation.  The reference's GEMM+bias+GELU is fp32-only
  * (gemm_bias_gelu.cuh:5); this is its bf16 tensor-core counterpart. */
 int cuda_operator_gemm_bias_gelu_bf16(const void* input_bf16, const void* weight_bf16, const float* bias, void* output_bf16, uint64_t m, uint64_t k, uint64_t n, void* stream);
+
+/* Down projection with the residual add fused: out[m, n] = bf16(x[m, :] . w[n, :]
+ * + residual[m, n]), fp32 accumulation, bf16 x[M, K], W[N, K], residual and
+ * out [M, N].  No reference counterpart: the step after GEMM+SwiGLU in a
+ * decoder MLP block (down projection back to the model width plus the block's
+ * residual).  out may equal residual (in-place update).  m == 0 or n == 0
+ * succeeds; NULL, k == 0 or sizes above INT32_MAX return cudaErrorInvalidValue. */
+int cuda_operator_gemm_residual_bf16(const void* input_bf16, const void* weight_bf16, const void* residual_bf16, void* output_bf16, uint64_t m, uint64_t k, uint64_t n, void* stream);
 
 /* Partial sum for the multi-GPU reduction: partial[0] = sum(input[0..n)) in
  * fp64, with the same partition and combine order as the fp32 entry points.

@@ -28,12 +28,16 @@ def _cpu_args(name: str):
         return [f32(2, 8), f32(8)]
     if name.startswith("layernorm"):
         return [f32(2, 8), f32(8), f32(8)]
+    if name.startswith("fused_residual_rmsnorm"):
+        return [f32(2, 8), f32(2, 8), f32(8)]
     if name.startswith("fused_residual_layernorm"):
         return [f32(2, 8), f32(2, 8), f32(8), f32(8)]
     if name.startswith("fused_bias_gelu"):
         return [f32(2, 8), f32(8)]
     if name.startswith("swiglu"):
         return [f32(2, 8), f32(2, 8)]
+    if name.startswith("gemm_residual_bf16"):
+        return [bf(2, 8), bf(4, 8), bf(2, 4)]
     if name.startswith("gemm_bias_gelu_bf16"):
         return [bf(2, 8), bf(4, 8), f32(4)]
     if name.startswith("gemm_bias_gelu"):

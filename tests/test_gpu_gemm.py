@@ -189,6 +189,29 @@ def test_long_k_few_tiles(m, k, n):
     close(out, oracle.gemm_bias_gelu(x.float(), wg.float(), bias), BF_RTOL, BF_ATOL)
 
 
+@pytest.mark.parametrize(("m", "k", "n"), [(1, 8, 1), (16, 64, 64), (100, 256, 300),
+                                           (512, 14336, 4096), (257, 520, 1000), (3, 30, 5),
+                                           (1024, 4096, 4096)])
+def test_gemm_residual_bf16(m, k, n):
+    g = seeded(20261210 + m + k + n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * k ** -0.5).to(torch.bfloat16)
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    actual = b.gemm_residual_bf16(x.to(DEV), w.to(DEV), res.to(DEV))
+    close(actual, oracle.gemm_residual_bf16(x, w, res), BF_RTOL, BF_ATOL)
+
+
+def test_gemm_residual_bf16_in_place():
+    g = seeded(20261211)
+    m, k, n = 384, 1024, 768
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(n, k, generator=g) * k ** -0.5).to(torch.bfloat16).to(DEV)
+    h = torch.randn(m, n, generator=g).to(torch.bfloat16).to(DEV)
+    expected = oracle.gemm_residual_bf16(x.cpu(), w.cpu(), h.cpu())
+    b.gemm_residual_bf16_into(x, w, h, h)  # h += x @ w.T
+    close(h, expected, BF_RTOL, BF_ATOL)
+
+
 def test_gemm_golden_cases(golden):
     seen = 0
     for case in golden:

@@ -1,5 +1,6 @@
 """Parity of the row-wise kernels (RMSNorm, LayerNorm, residual+LayerNorm,
-softmax) with the CPU oracle and the reference's golden outputs (GPU).
+residual+RMSNorm, softmax) with the CPU oracle and the reference's golden
+outputs (GPU).
 
 Shapes follow the reference's tests (tests/test_rmsnorm_v0.py:16-32,
 tests/test_softmax_v2.py:16-41): empty, single element, widths around the
@@ -9,6 +10,8 @@ kernel).  Tolerance: BASELINE's fp32 bar, rtol 1e-5 / atol 1e-6.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import pytest
 import torch
@@ -23,7 +26,7 @@ RTOL, ATOL = 1e-5, 1e-6
 SHAPES = [(0, 128), (1, 1), (1, 3), (2, 31), (2, 32), (2, 33), (7, 127), (64, 128), (33, 512),
           (17, 1024), (8, 4097), (11, 257), (32, 4096), (128, 4096), (128, 8192), (5, 12289),
           (3, 33000), (2, 40000),
-          # cluster path (few rows, 513..4096 vectors): partial, empty and full last CTA
+          # few wide rows, 8 vectors per thread, and more rows than SMs
           (3, 2052), (7, 6144), (100, 16384), (296, 4096)]
 DEV = "cuda"
 
@@ -112,6 +115,51 @@ def test_residual_layernorm_h_stores_sum_and_norm(rows, cols):
     h_ref, y_ref = oracle.fused_residual_layernorm_h(x, r, w, bias)
     close(h, h_ref, rtol=0, atol=0)
     close(y, y_ref)
+
+
+@pytest.mark.parametrize(("rows", "cols"), SHAPES)
+def test_residual_rmsnorm_fp32_stores_sum_and_norm(rows, cols):
+    g = seeded(20261208 + rows * 10000 + cols)
+    x = torch.randn(rows, cols, generator=g)
+    r = torch.randn(rows, cols, generator=g)
+    w = torch.rand(cols, generator=g) + 0.5
+    h, y = b.fused_residual_rmsnorm(x.to(DEV), r.to(DEV), w.to(DEV), 1e-6)
+    h_ref, y_ref = oracle.fused_residual_rmsnorm(x, r, w, 1e-6)
+    close(h, h_ref, rtol=0, atol=0)
+    close(y, y_ref)
+
+
+@pytest.mark.parametrize(("rows", "cols"), [(0, 64), (1, 1), (3, 100), (16384 // 64, 4096),
+                                            (7, 4104), (5, 2000), (2, 70000)])
+def test_residual_rmsnorm_bf16_stores_sum_and_norm(rows, cols):
+    g = seeded(20261209 + rows + cols)
+    x = torch.randn(rows, cols, generator=g).to(torch.bfloat16)
+    r = torch.randn(rows, cols, generator=g).to(torch.bfloat16)
+    w = (torch.rand(cols, generator=g) + 0.5).to(torch.bfloat16)
+    h, y = b.fused_residual_rmsnorm(x.to(DEV), r.to(DEV), w.to(DEV), 1e-6)
+    h_ref, y_ref = oracle.fused_residual_rmsnorm(x, r, w, 1e-6)
+    torch.cuda.synchronize()
+    # h: one bf16 add, bit for bit; y: within one bf16 rounding step
+    assert torch.equal(h.cpu(), h_ref)
+    torch.testing.assert_close(y.cpu().float(), y_ref.float(), rtol=2 ** -7, atol=1e-6)
+
+
+def test_residual_rmsnorm_argument_checks():
+    x = torch.randn(4, 64, device=DEV)
+    w = torch.ones(64, device=DEV)
+    with pytest.raises(ValueError):
+        b.fused_residual_rmsnorm(x, x[:, :32].contiguous(), w)
+    with pytest.raises(ValueError):
+        b.fused_residual_rmsnorm(x, x, w, eps=0.0)
+    out = torch.empty_like(x)
+    P, U, F = ctypes.c_void_p, ctypes.c_uint64, ctypes.c_float
+    lib = b._library()
+    # rows == 0 succeeds before pointer checks; a NULL pointer is invalid (1)
+    assert lib.handle.cuda_operator_fused_residual_rmsnorm_h(
+        None, None, None, None, None, U(0), U(64), F(1e-5), None) == 0
+    assert lib.handle.cuda_operator_fused_residual_rmsnorm_h(
+        P(x.data_ptr()), None, P(w.data_ptr()), P(out.data_ptr()), P(out.data_ptr()), U(4), U(64),
+        F(1e-5), None) == 1
 
 
 @pytest.mark.parametrize("version", range(6))
