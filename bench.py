@@ -498,6 +498,23 @@ def run_ours(args, d: Dist) -> dict | None:
     if status != 0:
         raise RuntimeError(f"GEMM bounded wait timed out (status {status})")
 
+    # the same block with the RMSNorm folded into the GEMM: norm weight folded into
+    # W once (weight preparation, like packing), then per step a per-row rstd pass
+    # over X and the GEMM applying rstd in its epilogue -- no normalised X written
+    # or re-read
+    folded = b.fold_rmsnorm_weight(packed, w_norm)
+    rstd = torch.empty(M, device=dev)
+
+    def folded_step():
+        b.rmsnorm_rstd_bf16_into(x, rstd, EPS)
+        b.gemm_swiglu_rowscale_bf16_into(x, rstd, folded, out)
+
+    b.gemm_status(clear=True)
+    fold_ms = time_region(d, folded_step, args.steps, args.warmup)
+    if b.gemm_status(clear=True) != 0:
+        raise RuntimeError("GEMM bounded wait timed out in the folded step")
+    del folded
+
     # dominant kernel alone: average GEMM launch duration
     gemm_steps = max(10, args.steps // 2)
     gemm_ms = time_region(d, lambda: b.gemm_swiglu_bf16_into(xn, packed, out), gemm_steps, 3)
@@ -559,6 +576,10 @@ def run_ours(args, d: Dist) -> dict | None:
                      "peak_source": f"{pk['source']} sustained bf16",
                      "gemm_us_per_launch": round(gemm_us, 2)},
         "cpu_baseline": cpu,
+        "variants": {"rmsnorm_folded_into_gemm": {
+            "value": round(GEMM_FLOPS * args.steps / (fold_ms / 1e3) / 1e12, 2),
+            "ms_per_step": round(fold_ms / args.steps, 4),
+            "step": "rmsnorm_rstd_bf16 + gemm_swiglu_rowscale_bf16 (norm weight folded into W)"}},
         "clocks": clock_info,
         "gpu_launches": 2 * args.steps,
         "ops": ops,

@@ -223,7 +223,7 @@ bool flush_wide_ok(bool pair) {
 template <int EPI, typename TOut, bool FLUSH = false>
 int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, void* out,
                        std::uint64_t m, std::uint64_t n, cudaStream_t s,
-                       const void* residual = nullptr) {
+                       const void* residual = nullptr, const float* row_scale = nullptr) {
   int dev = 0;
   const col::DeviceInfo& info = col::device_info(&dev);
   if (info.cc_major != 10) return col::kErrDeviceNotSupported;
@@ -255,6 +255,7 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
   if (rc != 0) return rc;
   p.bias = bias;
   p.residual = residual;
+  p.row_scale = row_scale;
   p.out = out;
   p.status = status;
   p.m = static_cast<int>(m);
@@ -323,14 +324,14 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
 template <int EPI, typename TOut>
 int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, const float* bias,
                  void* out, std::uint64_t m, std::uint64_t n, std::uint64_t k, cudaStream_t s,
-                 const void* residual = nullptr) {
+                 const void* residual = nullptr, const float* row_scale = nullptr) {
   if ((k % 8) != 0 || !col::aligned16(x) || !col::aligned16(w0) ||
       (mode == BMode::kSwiGLU && !col::aligned16(w1))) {
     return -1;
   }
   TcOperands ops{x, k, w0, mode == BMode::kSwiGLU ? w1 : w0, n, k,
                  static_cast<int>((k + col::sm100::kBlockK - 1) / col::sm100::kBlockK), 0, 0u};
-  return launch_tensor_gemm<EPI, TOut>(ops, mode, bias, out, m, n, s, residual);
+  return launch_tensor_gemm<EPI, TOut>(ops, mode, bias, out, m, n, s, residual, row_scale);
 }
 
 // ---------------------------------------------------------------- fp32 on tensor cores
@@ -432,8 +433,10 @@ int gemm_fp32_tc(const float* x, const float* w0, const float* w1, BMode mode, c
 template <typename TIn, int EPI, typename TOut>
 int gemm_simt(const void* x, const void* w0, const void* w1, const float* bias, void* out,
               std::uint64_t m, std::uint64_t n, std::uint64_t k, cudaStream_t s,
-              const void* residual = nullptr) {
-  col::simt::SimtParams p{x, w0, w1, bias, residual, out, static_cast<int>(m), static_cast<int>(n),
+              const void* residual = nullptr, const float* row_scale = nullptr) {
+  col::simt::SimtParams p{x,        w0,  w1,
+                          bias,     residual, row_scale,
+                          out,      static_cast<int>(m), static_cast<int>(n),
                           static_cast<int>(k)};
   return col::simt::launch_simt<TIn, EPI, TOut>(p, s);
 }
@@ -675,6 +678,32 @@ COL_API int cuda_operator_gemm_residual_bf16(const void* input_bf16, const void*
   if (rc != -1) return rc;
   return gemm_simt<__nv_bfloat16, col::sm100::kEpiResidual, __nv_bfloat16>(
       input_bf16, weight_bf16, nullptr, nullptr, output_bf16, m, n, k, s, residual_bf16);
+}
+
+// Packed GEMM + SwiGLU with the RMSNorm of x folded in (no reference
+// counterpart): out[m, j] = bf16(silu(rs[m] * g) * (rs[m] * u)) where g and u
+// are the fp32-accumulated products of the raw bf16 x with the packed weight,
+// whose columns the caller has already multiplied by the RMSNorm weight, and
+// rs[m] = rsqrt(mean(x[m]^2) + eps) (cuda_operator_rmsnorm_rstd_bf16).  Since
+// (x * rs * w) . W^T = rs * (x . (W * w)^T), this is the RMSNorm -> GEMM+SwiGLU
+// block without writing or re-reading the normalised activations.
+COL_API int cuda_operator_gemm_swiglu_rowscale_bf16(const void* input_bf16, const float* row_scale,
+                                                    const void* packed_weight_bf16,
+                                                    void* output_bf16, uint64_t m, uint64_t k,
+                                                    uint64_t n, void* stream) {
+  if (m == 0 || n == 0) return 0;
+  if (!input_bf16 || !row_scale || !packed_weight_bf16 || !output_bf16 ||
+      !dims_ok(m, n, k, 0x7fffffffull / 2)) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  const cudaStream_t s = col::as_stream(stream);
+  const void* wu = up_half(packed_weight_bf16, n, k, 2);
+  const int rc = gemm_bf16_tc<col::sm100::kEpiSwiGLURowScale, __nv_bfloat16>(
+      input_bf16, packed_weight_bf16, wu, BMode::kSwiGLU, nullptr, output_bf16, m, n, k, s, nullptr,
+      row_scale);
+  if (rc != -1) return rc;
+  return gemm_simt<__nv_bfloat16, col::sm100::kEpiSwiGLURowScale, __nv_bfloat16>(
+      input_bf16, packed_weight_bf16, wu, nullptr, output_bf16, m, n, k, s, nullptr, row_scale);
 }
 
 COL_API int cuda_operator_lab_gemm_status(unsigned int* status, int clear) {

@@ -31,6 +31,7 @@ struct SimtParams {
   const void* b1;   // up rows [N, K] (SwiGLU only)
   const float* bias;
   const void* residual;  // kEpiResidual: bf16 [M, N]
+  const float* row_scale;  // kEpiSwiGLURowScale: fp32 [M]
   void* out;        // [M, N]
   int m;
   int n;
@@ -48,7 +49,8 @@ __device__ __forceinline__ float load_elem(const T* p, std::size_t i) {
 
 template <typename TIn, int EPI, typename TOut>
 __global__ void __launch_bounds__(kThreads) simt_gemm_kernel(const SimtParams p) {
-  constexpr bool kSwiGLU = (EPI == sm100::kEpiSwiGLU || EPI == sm100::kEpiSwiGLURoundBf16);
+  constexpr bool kSwiGLU = (EPI == sm100::kEpiSwiGLU || EPI == sm100::kEpiSwiGLURoundBf16 ||
+                           EPI == sm100::kEpiSwiGLURowScale);
   __shared__ float As[kBK][kBM + 4];
   __shared__ float Bs0[kBK][kBN + 4];
   __shared__ float Bs1[kSwiGLU ? kBK : 1][kSwiGLU ? kBN + 4 : 1];
@@ -116,6 +118,9 @@ __global__ void __launch_bounds__(kThreads) simt_gemm_kernel(const SimtParams p)
       float o;
       if constexpr (EPI == sm100::kEpiSwiGLU) {
         o = silu_f(accg[i][j]) * accu[i][j];
+      } else if constexpr (EPI == sm100::kEpiSwiGLURowScale) {
+        const float rs = __ldg(p.row_scale + gm);
+        o = silu_f(accg[i][j] * rs) * (accu[i][j] * rs);
       } else if constexpr (EPI == sm100::kEpiSwiGLURoundBf16) {
         o = silu_f(bf16_round(accg[i][j])) * bf16_round(accu[i][j]);
       } else if constexpr (EPI == sm100::kEpiResidual) {

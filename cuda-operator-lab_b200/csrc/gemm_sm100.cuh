@@ -41,6 +41,7 @@ enum Epilogue : int {
   kEpiBiasGeluErf = 2,      // out = gelu_erf(acc + bias[n])
   kEpiBiasGeluTanh = 3,     // out = gelu_tanh(acc + bias[n])
   kEpiResidual = 4,         // out = acc + residual[m, n] (bf16 residual, down projection)
+  kEpiSwiGLURowScale = 5,   // g, u scaled by row_scale[m] first (RMSNorm folded into the GEMM)
 };
 
 constexpr int kBlockM = 128;
@@ -63,6 +64,7 @@ struct __align__(64) GemmParams {
   CUtensorMap map_b1;  // up rows (SwiGLU) or W rows (GELU)
   const float* bias;
   const void* residual;  // kEpiResidual: bf16 [m, n], row stride out_ld (may equal out)
+  const float* row_scale;  // kEpiSwiGLURowScale: fp32 [m]
   void* out;
   unsigned* status;
   int m;
@@ -491,8 +493,10 @@ __device__ __forceinline__ void load_residual16(const GemmParams& p, int row, in
 template <int BNH, int EPI, typename TOut>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int row, int nb, uint32_t t_row,
                                               int group) {
-  if constexpr (EPI == kEpiSwiGLU || EPI == kEpiSwiGLURoundBf16) {
+  if constexpr (EPI == kEpiSwiGLU || EPI == kEpiSwiGLURoundBf16 || EPI == kEpiSwiGLURowScale) {
     const int col_base = nb * BNH;
+    float rs = 1.0f;
+    if constexpr (EPI == kEpiSwiGLURowScale) rs = row < p.m ? __ldg(p.row_scale + row) : 0.0f;
 #pragma unroll 1
     for (int c = group * 16; c < BNH; c += 16 * kEpiGroups) {
       uint32_t g[16], u[16];
@@ -505,6 +509,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int row, int 
         if constexpr (EPI == kEpiSwiGLURoundBf16) {
           gv = bf16_round(gv);
           uv = bf16_round(uv);
+        } else if constexpr (EPI == kEpiSwiGLURowScale) {
+          gv *= rs;
+          uv *= rs;
         }
         o[j] = silu_fast(gv) * uv;
       }

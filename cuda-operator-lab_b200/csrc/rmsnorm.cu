@@ -89,3 +89,19 @@ COL_API int cuda_operator_fused_residual_rmsnorm_h(const float* input, const flo
                                                    float eps, void* stream) {
   return residual_rmsnorm<float>(input, residual, weight, h_out, output, rows, cols, eps, stream);
 }
+
+// Per-row inverse RMS of a bf16 matrix, rstd[row] = rsqrt(mean(x[row]^2) + eps)
+// in fp32 (no reference counterpart): the statistics half of RMSNorm, for
+// cuda_operator_gemm_swiglu_rowscale_bf16, which applies it in the GEMM's
+// epilogue.  Reads x once, writes 4 bytes per row.
+COL_API int cuda_operator_rmsnorm_rstd_bf16(const void* input_bf16, float* rstd, uint64_t rows,
+                                            uint64_t cols, float eps, void* stream) {
+  if (rows == 0) return 0;
+  if (input_bf16 == nullptr || rstd == nullptr || !col::row_dims_ok(rows, cols)) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  if (!(eps > 0.0f)) return static_cast<int>(cudaErrorInvalidValue);
+  col::RowArgs a{input_bf16, nullptr, nullptr, nullptr, rstd, nullptr, rows,
+                 static_cast<std::uint32_t>(cols), eps};
+  return col::launch_rows<col::RowOp::kRmsRstd, __nv_bfloat16, false>(a, col::as_stream(stream));
+}

@@ -25,6 +25,7 @@ enum class RowOp : int {
   kResidualLayerNorm = 2,
   kSoftmax = 3,
   kResidualRms = 4,
+  kRmsRstd = 5,  // only rsqrt(mean(x^2) + eps) per row, as fp32 into y[row]
 };
 
 // Ops that normalise h = x + residual (and may store h).
@@ -202,7 +203,15 @@ row_kernel(const RowArgs a) {
   T* __restrict__ y = static_cast<T*>(a.y) + base;
   const float inv_cols = 1.0f / static_cast<float>(cols);
 
-  if constexpr (OP == RowOp::kRms || OP == RowOp::kResidualRms) {
+  if constexpr (OP == RowOp::kRmsRstd) {
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) s = fmaf(v[j][e], v[j][e], s);
+    s = group_sum<TPR>(s, sh);
+    if (row_ok && t == 0) static_cast<float*>(a.y)[row] = rsqrtf(s * inv_cols + a.eps);
+  } else if constexpr (OP == RowOp::kRms || OP == RowOp::kResidualRms) {
     // Weights are loaded before the reduction so their latency overlaps it
     // (when the registers allow: up to 16 elements per thread).
     constexpr bool kEarly = NV * VEC <= 16;
@@ -399,7 +408,15 @@ __global__ void __launch_bounds__(kLongThreads) row_kernel_long(const RowArgs a)
     }
   };
 
-  if constexpr (OP == RowOp::kRms || OP == RowOp::kResidualRms) {
+  if constexpr (OP == RowOp::kRmsRstd) {
+    float s = 0.0f;
+    for (std::uint32_t i = threadIdx.x; i < cols; i += kLongThreads) {
+      const float v = in(i);
+      s = fmaf(v, v, s);
+    }
+    const float rstd = rsqrtf(block_sum_long(s, sh) * inv_cols + a.eps);
+    if (threadIdx.x == 0) static_cast<float*>(a.y)[row] = rstd;
+  } else if constexpr (OP == RowOp::kRms || OP == RowOp::kResidualRms) {
     float s = 0.0f;
     for (std::uint32_t i = threadIdx.x; i < cols; i += kLongThreads) {
       const float v = in(i);
@@ -474,6 +491,7 @@ inline int launch_rows(const RowArgs& a, cudaStream_t s) {
   if (has_residual(OP)) vec = vec && aligned16(a.residual);
   if (STORE_H) vec = vec && aligned16(a.h);
   if (OP == RowOp::kSoftmax) vec = (a.cols % kVec) == 0 && aligned16(a.x) && aligned16(a.y);
+  if (OP == RowOp::kRmsRstd) vec = (a.cols % kVec) == 0 && aligned16(a.x);
   if (vec) return dispatch_row_width<OP, T, kVec, STORE_H>(a.cols / kVec, a, s);
   return dispatch_row_width<OP, T, 1, STORE_H>(a.cols, a, s);
 }

@@ -16,7 +16,8 @@ There is no fallback: if the shared library is missing, the first call raises
 
 Functions after the reference set (``rmsnorm_bf16``, ``fused_residual_layernorm_h``,
 ``fused_residual_rmsnorm``, ``gemm_swiglu_bf16``, ``gemm_bias_gelu_bf16``,
-``gemm_residual_bf16``, ``reduction_partial_f64``) expose the library's additional entry points.
+``gemm_residual_bf16``, ``rmsnorm_rstd_bf16``, ``gemm_swiglu_rowscale_bf16``,
+``reduction_partial_f64``) expose the library's additional entry points.
 """
 
 from __future__ import annotations
@@ -71,6 +72,8 @@ _SIGNATURES["cuda_operator_fused_residual_rmsnorm_h"] = [_P, _P, _P, _P, _P, _U6
 _SIGNATURES["cuda_operator_gemm_swiglu_bf16"] = [_P, _P, _P, _U64, _U64, _U64, _P]
 _SIGNATURES["cuda_operator_gemm_bias_gelu_bf16"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
 _SIGNATURES["cuda_operator_gemm_residual_bf16"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
+_SIGNATURES["cuda_operator_rmsnorm_rstd_bf16"] = [_P, _P, _U64, _U64, _F32, _P]
+_SIGNATURES["cuda_operator_gemm_swiglu_rowscale_bf16"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
 _SIGNATURES["cuda_operator_reduction_partial_f64"] = [_P, _P, _U64, _P]
 _SIGNATURES["cuda_operator_lab_device_info"] = [_P, _P, _P]
 _SIGNATURES["cuda_operator_lab_build_tag"] = []
@@ -740,6 +743,88 @@ def gemm_residual_bf16(x_bf16: torch.Tensor, weight_bf16: torch.Tensor,
 
 
 __all__ += ["gemm_residual_bf16_into", "gemm_residual_bf16"]
+
+# ---------------------------------------------------------------- RMSNorm folded into the GEMM
+
+
+def rmsnorm_rstd_bf16_into(x_bf16: torch.Tensor, rstd: torch.Tensor,
+                           eps: float = 1e-5) -> torch.Tensor:
+    """Per-row inverse RMS of bf16 x: rstd[row] = rsqrt(mean(x[row]^2) + eps), fp32."""
+    if not x_bf16.is_cuda or not rstd.is_cuda:
+        raise ValueError("rmsnorm input and rstd must be CUDA tensors")
+    if x_bf16.ndim != 2 or x_bf16.dtype != torch.bfloat16 or not x_bf16.is_contiguous():
+        raise ValueError("rmsnorm_rstd_bf16 expects a contiguous 2-D bfloat16 input")
+    if rstd.shape != (x_bf16.shape[0],) or rstd.dtype != torch.float32 or not rstd.is_contiguous():
+        raise ValueError("rstd must be a contiguous float32 vector of length rows")
+    if x_bf16.shape[1] == 0:
+        raise ValueError("rmsnorm requires cols > 0")
+    if eps <= 0:
+        raise ValueError("rmsnorm eps must be positive")
+    rows, cols = x_bf16.shape
+    if rows == 0:
+        return rstd
+    _call("cuda_operator_rmsnorm_rstd_bf16", _ptr(x_bf16), _ptr(rstd), ctypes.c_uint64(rows),
+          ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x_bf16))
+    return rstd
+
+
+def rmsnorm_rstd_bf16(x_bf16: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """Allocating form of :func:`rmsnorm_rstd_bf16_into`."""
+    return rmsnorm_rstd_bf16_into(
+        x_bf16, torch.empty(x_bf16.shape[0], device=x_bf16.device, dtype=torch.float32), eps)
+
+
+def fold_rmsnorm_weight(packed_weight_bf16: torch.Tensor,
+                        norm_weight_bf16: torch.Tensor) -> torch.Tensor:
+    """W * diag(w) for :func:`gemm_swiglu_rowscale_bf16`: every column k of the packed
+    [2N, K] weight multiplied by the RMSNorm weight w[k] (fp32 product, rounded once
+    to bf16).  A one-time weight transform, like packing."""
+    if packed_weight_bf16.ndim != 2 or norm_weight_bf16.shape != (packed_weight_bf16.shape[1],):
+        raise ValueError("norm weight length must equal the packed weight's K")
+    return (packed_weight_bf16.float() * norm_weight_bf16.float()[None, :]).to(torch.bfloat16)
+
+
+def gemm_swiglu_rowscale_bf16_into(x_bf16: torch.Tensor, row_scale: torch.Tensor,
+                                   packed_weight_bf16: torch.Tensor,
+                                   out_bf16: torch.Tensor) -> torch.Tensor:
+    """bf16(silu(rs * (x @ Wg.T)) * (rs * (x @ Wu.T))) with rs = row_scale[row]: the
+    RMSNorm -> GEMM+SwiGLU block when the weight was folded by :func:`fold_rmsnorm_weight`
+    and row_scale comes from :func:`rmsnorm_rstd_bf16`."""
+    tensors = (x_bf16, row_scale, packed_weight_bf16, out_bf16)
+    if not all(t.is_cuda for t in tensors):
+        raise ValueError("GEMM SwiGLU tensors must be CUDA tensors")
+    if x_bf16.ndim != 2 or packed_weight_bf16.ndim != 2:
+        raise ValueError("x and packed weight must be 2-D")
+    if x_bf16.shape[1] != packed_weight_bf16.shape[1] or packed_weight_bf16.shape[0] % 2:
+        raise ValueError("packed weight must be [2N, K] with K = x.shape[1]")
+    n = packed_weight_bf16.shape[0] // 2
+    m, k = x_bf16.shape
+    if row_scale.shape != (m,) or row_scale.dtype != torch.float32:
+        raise ValueError("row_scale must be a float32 vector of length M")
+    if out_bf16.shape != (m, n):
+        raise ValueError(f"output shape must be {(m, n)}")
+    if any(t.dtype != torch.bfloat16 for t in (x_bf16, packed_weight_bf16, out_bf16)):
+        raise TypeError("GEMM SwiGLU row-scale expects bfloat16 x, weight and output")
+    if not all(t.is_contiguous() for t in tensors):
+        raise ValueError("all GEMM SwiGLU tensors must be contiguous")
+    if m == 0 or n == 0:
+        return out_bf16
+    _call("cuda_operator_gemm_swiglu_rowscale_bf16", _ptr(x_bf16), _ptr(row_scale),
+          _ptr(packed_weight_bf16), _ptr(out_bf16), ctypes.c_uint64(m), ctypes.c_uint64(k),
+          ctypes.c_uint64(n), _stream(x_bf16))
+    return out_bf16
+
+
+def gemm_swiglu_rowscale_bf16(x_bf16: torch.Tensor, row_scale: torch.Tensor,
+                              packed_weight_bf16: torch.Tensor) -> torch.Tensor:
+    """Allocating form of :func:`gemm_swiglu_rowscale_bf16_into`."""
+    out = torch.empty((x_bf16.shape[0], packed_weight_bf16.shape[0] // 2), device=x_bf16.device,
+                      dtype=torch.bfloat16)
+    return gemm_swiglu_rowscale_bf16_into(x_bf16, row_scale, packed_weight_bf16, out)
+
+
+__all__ += ["rmsnorm_rstd_bf16_into", "rmsnorm_rstd_bf16", "fold_rmsnorm_weight",
+            "gemm_swiglu_rowscale_bf16_into", "gemm_swiglu_rowscale_bf16"]
 
 # ---------------------------------------------------------------- GEMM + SwiGLU
 # reference bindings.py:2036-2818

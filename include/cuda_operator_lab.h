@@ -164,6 +164,21 @@ int cuda_operator_fused_residual_layernorm_h(const float* input, const float* re
 int cuda_operator_fused_residual_rmsnorm_bf16(const void* input_bf16, const void* residual_bf16, const void* weight_bf16, void* h_out_bf16, void* output_bf16, uint64_t rows, uint64_t cols, float eps, void* stream);
 int cuda_operator_fused_residual_rmsnorm_h(const float* input, const float* residual, const float* weight, float* h_out, float* output, uint64_t rows, uint64_t cols, float eps, void* stream);
 
+/* Per-row inverse RMS of bf16 x[rows, cols]: rstd[row] = rsqrt(mean(x[row]^2) + eps)
+ * in fp32 (the statistics of references.py:46-47 without the scaling pass).
+ * No reference counterpart; pairs with cuda_operator_gemm_swiglu_rowscale_bf16.
+ * Same argument rules as cuda_operator_rmsnorm_bf16. */
+int cuda_operator_rmsnorm_rstd_bf16(const void* input_bf16, float* rstd, uint64_t rows, uint64_t cols, float eps, void* stream);
+
+/* RMSNorm -> packed GEMM+SwiGLU with the normalisation folded into the GEMM:
+ * out[m, j] = bf16(silu(rs[m] * g) * (rs[m] * u)), g and u the fp32-accumulated
+ * products of the raw bf16 x[M, K] with the packed weight [2N, K] whose columns
+ * the caller multiplied by the RMSNorm weight once (W * diag(w)), rs from
+ * cuda_operator_rmsnorm_rstd_bf16.  Equal to RMSNorm followed by
+ * cuda_operator_gemm_swiglu_bf16 up to bf16 rounding, without writing and
+ * re-reading the normalised activations.  No reference counterpart. */
+int cuda_operator_gemm_swiglu_rowscale_bf16(const void* input_bf16, const float* row_scale, const void* packed_weight_bf16, void* output_bf16, uint64_t m, uint64_t k, uint64_t n, void* stream);
+
 /* Packed GEMM + SwiGLU with bf16 output: out[m, j] = bf16(silu(g) * u), g and u
  * accumulated in fp32 from bf16 x[M, K] and packed W[2N, K].  Same arithmetic
  * as cuda_operator_gemm_swiglu_v4 up to the final rounding; no workspace. */

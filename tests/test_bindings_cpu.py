@@ -36,6 +36,10 @@ def _cpu_args(name: str):
         return [f32(2, 8), f32(8)]
     if name.startswith("swiglu"):
         return [f32(2, 8), f32(2, 8)]
+    if name.startswith("rmsnorm_rstd_bf16"):
+        return [bf(2, 8)]
+    if name.startswith("gemm_swiglu_rowscale_bf16"):
+        return [bf(2, 8), f32(2), bf(8, 8)]
     if name.startswith("gemm_residual_bf16"):
         return [bf(2, 8), bf(4, 8), bf(2, 4)]
     if name.startswith("gemm_bias_gelu_bf16"):
@@ -58,7 +62,8 @@ def _cpu_args(name: str):
 ALLOCATING_OPS = sorted(
     name for name in b.__all__
     if not name.endswith("_into") and callable(getattr(b, name))
-    and name not in ("gemm_status", "device_info", "build_tag", "library_path")
+    and name not in ("gemm_status", "device_info", "build_tag", "library_path",
+                     "fold_rmsnorm_weight")
 )
 
 

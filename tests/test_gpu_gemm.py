@@ -212,6 +212,26 @@ def test_gemm_residual_bf16_in_place():
     close(h, expected, BF_RTOL, BF_ATOL)
 
 
+@pytest.mark.parametrize(("m", "k", "n"), [(1, 8, 1), (100, 256, 300), (512, 4096, 4096),
+                                           (257, 520, 1000), (2048, 4096, 14336 // 8)])
+def test_rmsnorm_folded_into_gemm_swiglu(m, k, n):
+    g = seeded(20261213 + m + k + n)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w_norm = (torch.rand(k, generator=g) + 0.5).to(torch.bfloat16)
+    _, wg, wu = bf16_inputs(m, k, n, 20261214 + m + k + n)
+    packed = torch.cat((wg, wu), 0).contiguous()
+    folded = b.fold_rmsnorm_weight(packed, w_norm)
+    xd = x.to(DEV)
+    rstd = b.rmsnorm_rstd_bf16(xd, 1e-6)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(rstd.cpu(), oracle.rmsnorm_rstd(x, 1e-6), rtol=1e-5, atol=1e-7)
+    actual = b.gemm_swiglu_rowscale_bf16(xd, rstd, folded.to(DEV))
+    close(actual, oracle.gemm_swiglu_rowscale_bf16(x, rstd.cpu(), folded), BF_RTOL, BF_ATOL)
+    # and the unfused block it replaces: RMSNorm (bf16) then the packed GEMM+SwiGLU
+    unfused = oracle.gemm_swiglu_bf16_fp32_reference(oracle.rmsnorm_bf16(x, w_norm, 1e-6), packed)
+    close(actual, unfused, 3e-2, 3e-2)
+
+
 def test_gemm_golden_cases(golden):
     seen = 0
     for case in golden:
