@@ -537,7 +537,7 @@ def run_ours(args, d: Dist) -> dict | None:
 
     flops_launch = 2 * M * K * 2 * n_local
     achieved = flops_launch / gemm_us / 1e6
-    traffic = committed_traffic().get(f"gemm_swiglu_bf16_M{M}_K{K}_N{n_local}")
+    traffic = committed_traffic().get(f"gemm_swiglu_rowscale_bf16_M{M}_K{K}_N{n_local}")
 
     # e2e through the public API: pinned host X in, output shard back, every step
     x_host = x.cpu().pin_memory()
@@ -684,7 +684,7 @@ def run_reference(args) -> dict:
 KERNEL_CASES = ("gemm_swiglu_bf16", "gemm_bias_gelu_bf16", "rmsnorm_bf16", "reduction",
                 "rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "bias_gelu_fp32", "swiglu_fp32",
                 "gemm_bias_gelu_fp32", "gemm_swiglu_fp32", "residual_rmsnorm_bf16",
-                "gemm_residual_bf16")
+                "gemm_residual_bf16", "gemm_swiglu_rowscale_bf16")
 
 
 def run_kernel_case(spec: str, reps: int, timed: bool = False) -> None:
@@ -726,6 +726,12 @@ def run_kernel_case(spec: str, reps: int, timed: bool = False) -> None:
         w = (torch.rand(c, device=dev, generator=g) + 0.5).bfloat16()
         h, y = torch.empty_like(x), torch.empty_like(x)
         fn = lambda: b.fused_residual_rmsnorm_into(x, res, w, h, y, EPS)  # noqa: E731
+    elif name == "gemm_swiglu_rowscale_bf16":
+        m, k, n = d or (M, K, N)
+        x, w = rn(m, k).bfloat16(), (rn(2 * n, k) * k ** -0.5).bfloat16()
+        rs = torch.rand(m, device=dev, generator=g) + 0.5
+        out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        fn = lambda: b.gemm_swiglu_rowscale_bf16_into(x, rs, w, out)  # noqa: E731
     elif name == "gemm_residual_bf16":
         m, k, n = d or (512, 14336, 4096)
         x, w = rn(m, k).bfloat16(), (rn(n, k) * k ** -0.5).bfloat16()
