@@ -119,11 +119,9 @@ __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
-// Streaming 16-byte loads/stores (read-once inputs, write-once outputs).
+// Streaming (evict-first) 16-byte load for read-once inputs whose data is not
+// needed again (the global reduction).
 __device__ __forceinline__ float4 ld_stream_f4(const float4* p) { return __ldcs(p); }
-__device__ __forceinline__ uint4 ld_stream_u4(const uint4* p) { return __ldcs(p); }
-__device__ __forceinline__ void st_stream_f4(float4* p, float4 v) { __stcs(p, v); }
-__device__ __forceinline__ void st_stream_u4(uint4* p, uint4 v) { __stcs(p, v); }
 
 __device__ __forceinline__ void unpack_bf16x8(uint4 v, float (&f)[8]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
