@@ -275,6 +275,17 @@ def test_tensor_core_path_is_exact_on_integer_inputs():
     torch.testing.assert_close(actual, expected, rtol=1e-6, atol=1e-5)
 
 
+def test_packed_versions_agree_bit_for_bit():
+    # reference tests/test_gemm_swiglu_v11.py:51 (v11 equals v10 exactly); here
+    # every packed bf16 version with fp32 output runs the same kernel
+    x, wg, wu = bf16_inputs(384, 1024, 768, 91)
+    packed = torch.cat((wg, wu), 0).contiguous().to(DEV)
+    xd = x.to(DEV)
+    v4, v10, v11 = (getattr(b, f"gemm_swiglu_v{v}")(xd, packed) for v in (4, 10, 11))
+    torch.cuda.synchronize()
+    assert torch.equal(v10, v11) and torch.equal(v4, v11)
+
+
 def test_gemm_repeated_calls_are_bitwise_stable():
     x, wg, wu = bf16_inputs(512, 1024, 1024, 77)
     packed = torch.cat((wg, wu), 0).contiguous().to(DEV)
