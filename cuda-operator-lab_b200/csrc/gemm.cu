@@ -67,7 +67,7 @@ int encode_bf16_rows(CUtensorMap* map, const void* base, std::uint64_t rows, std
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>
 int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
-  using Cfg = TileCfg<BNH>;
+  using Cfg = TileCfg<BNH, FLUSH ? 1 : 2>;
   auto kernel = col::sm100::gemm_bf16_tc_kernel<BNH, EPI, TOut, FLUSH>;
   static std::atomic<std::uint64_t> attr_set{0};
   const std::uint64_t bit = 1ull << (dev & 63);
@@ -89,7 +89,7 @@ int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
 // the answer).  Queried once per device; 0 if clusters are unavailable.
 template <int EPI, typename TOut>
 int max_pair_clusters(int dev) {
-  using Cfg = col::sm100::TileCfg2<128>;
+  using Cfg = col::sm100::TileCfg2<128, 2>;
   static int cached[64] = {};
   static std::once_flag flags[64];
   std::call_once(flags[dev & 63], [dev]() {
@@ -117,7 +117,7 @@ int max_pair_clusters(int dev) {
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>
 int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
-  using Cfg = col::sm100::TileCfg2<BNH>;
+  using Cfg = col::sm100::TileCfg2<BNH, FLUSH ? 1 : 2>;
   auto kernel = col::sm100::gemm_bf16_tc2_kernel<BNH, EPI, TOut, FLUSH>;
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int grid = 2 * (tiles < clusters ? tiles : clusters);
@@ -128,7 +128,7 @@ int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>
 int set_smem_attr_2sm(int dev) {
-  using Cfg = col::sm100::TileCfg2<BNH>;
+  using Cfg = col::sm100::TileCfg2<BNH, FLUSH ? 1 : 2>;
   static std::atomic<std::uint64_t> attr_set{0};
   const std::uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set.load(std::memory_order_acquire) & bit)) {

@@ -146,13 +146,19 @@ __host__ __device__ constexpr uint32_t pow2_at_least(uint32_t v) {
 // BNH = rows of each B box (gate/up half, or half of the GELU tile); the MMA
 // is M=128 x N=2*BNH.  BNH must keep the box a whole number of 1024-byte
 // swizzle atoms (BNH % 8 == 0) and 2*BNH a multiple of 16 in [16, 256].
-template <int BNH>
+// KPS = k-blocks per pipeline stage: the producer/MMA handshake of a stage
+// (barrier wait, commit) costs ~0.13 us that does not overlap the MMAs
+// (measured), so stages of two k-blocks halve it per k-block; the FLUSH
+// kernels keep one k-block per stage (their chunk boundaries).
+template <int BNH, int KPS = 1>
 struct TileCfg {
   static_assert(BNH % 16 == 0 && BNH >= 32 && BNH <= 128, "unsupported B box height");
+  static_assert(KPS == 1 || KPS == 2, "one or two k-blocks per stage");
   static constexpr int kMmaN = 2 * BNH;
   static constexpr uint32_t kABytes = kBlockM * kBlockK * 2;
   static constexpr uint32_t kBBytes = kMmaN * kBlockK * 2;
-  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kKBlockBytes = kABytes + kBBytes;  // [A | B] of one k-block
+  static constexpr uint32_t kStageBytes = KPS * kKBlockBytes;
   static constexpr uint32_t kBarrierBytes = 256;
   static constexpr int kStagesFit = static_cast<int>((kSmemLimit - 1024 - kBarrierBytes) / kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
@@ -640,7 +646,8 @@ __device__ __forceinline__ void epilogue_sums(const GemmParams& p, int row, int 
 
 template <int BNH, int EPI, typename TOut, bool FLUSH = false>
 __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
-  using Cfg = TileCfg<BNH>;
+  constexpr int kKps = FLUSH ? 1 : 2;
+  using Cfg = TileCfg<BNH, kKps>;
   constexpr int kStages = Cfg::kStages;
   constexpr uint32_t kIdesc = idesc_bf16_f32(kBlockM, Cfg::kMmaN);
 
@@ -714,7 +721,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
           const int a_row = mb * kBlockM;
           const int b0_row = nb * p.b_row_stride;
           const int b1_row = b0_row + p.b1_row_offset;
-          for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          for (int kb = 0; kb < p.num_k_blocks; kb += kKps) {
             // The first pass over the ring needs no wait (every slot starts
             // empty), and skipping it saves the first wait on a barrier just
             // initialised (~0.4 us measured), which a one-k-block tile feels.
@@ -724,15 +731,18 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
               ok = false;
               break;
             }
-            const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
-            const uint32_t sb = sa + Cfg::kABytes;
+            const int nk = min(kKps, p.num_k_blocks - kb);
             const uint32_t fb = smem_u32(full_bar + stage);
-            mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-            int ax, kx;
-            k_block_coords(p, kb, ax, kx);
-            tma_load_2d(sa, &p.map_a, fb, ax, a_row);
-            tma_load_2d(sb, &p.map_b0, fb, kx, b0_row);
-            tma_load_2d(sb + BNH * 128, &p.map_b1, fb, kx, b1_row);
+            mbar_arrive_expect_tx(fb, nk * Cfg::kKBlockBytes);
+            for (int j = 0; j < nk; ++j) {
+              const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes + j * Cfg::kKBlockBytes);
+              const uint32_t sb = sa + Cfg::kABytes;
+              int ax, kx;
+              k_block_coords(p, kb + j, ax, kx);
+              tma_load_2d(sa, &p.map_a, fb, ax, a_row);
+              tma_load_2d(sb, &p.map_b0, fb, kx, b0_row);
+              tma_load_2d(sb + BNH * 128, &p.map_b1, fb, kx, b1_row);
+            }
             if (filled < kStages) ++filled;
             issued_mask |= 1u << stage;
             issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
@@ -775,19 +785,22 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
             const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
             int kb0, kb1;
             chunk_range<FLUSH>(p, c, kb0, kb1);
-            for (int kb = kb0; kb < kb1; ++kb) {
+            for (int kb = kb0; kb < kb1; kb += kKps) {
               if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
                 fail(kStatusMma);
                 ok = false;
                 break;
               }
               tc_fence_after();
-              const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
-              const uint32_t sb = sa + Cfg::kABytes;
+              const int nk = min(kKps, kb1 - kb);
+              for (int j = 0; j < nk; ++j) {
+                const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes + j * Cfg::kKBlockBytes);
+                const uint32_t sb = sa + Cfg::kABytes;
 #pragma unroll
-              for (int k = 0; k < kBlockK / 16; ++k) {
-                umma_bf16(d_tmem, sdesc_kmajor_sw128(sa + k * 32), sdesc_kmajor_sw128(sb + k * 32),
-                          kIdesc, (kb != kb0 || k != 0) ? 1u : 0u);
+                for (int k = 0; k < kBlockK / 16; ++k) {
+                  umma_bf16(d_tmem, sdesc_kmajor_sw128(sa + k * 32), sdesc_kmajor_sw128(sb + k * 32),
+                            kIdesc, (kb + j != kb0 || k != 0) ? 1u : 0u);
+                }
               }
               issued_any = true;
               umma_commit(smem_u32(empty_bar + stage));

@@ -25,14 +25,17 @@
 namespace col {
 namespace sm100 {
 
-template <int BNH>
+// KPS = k-blocks per pipeline stage, as in TileCfg.
+template <int BNH, int KPS = 1>
 struct TileCfg2 {
   static_assert(BNH % 16 == 0 && BNH >= 32 && BNH <= 128, "unsupported B box height");
+  static_assert(KPS == 1 || KPS == 2, "one or two k-blocks per stage");
   static constexpr int kMmaM = 256;
   static constexpr int kMmaN = 2 * BNH;
   static constexpr uint32_t kABytes = kBlockM * kBlockK * 2;  // this CTA's 128 rows
   static constexpr uint32_t kBBytes = BNH * kBlockK * 2;      // this CTA's half of B
-  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kKBlockBytes = kABytes + kBBytes;  // [A | B] of one k-block
+  static constexpr uint32_t kStageBytes = KPS * kKBlockBytes;
   static constexpr uint32_t kBarrierBytes = 256;
   static constexpr int kStagesFit = static_cast<int>((kSmemLimit - 1024 - kBarrierBytes) / kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
@@ -118,7 +121,8 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols)
 template <int BNH, int EPI, typename TOut, bool FLUSH = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ GemmParams p) {
-  using Cfg = TileCfg2<BNH>;
+  constexpr int kKps = FLUSH ? 1 : 2;
+  using Cfg = TileCfg2<BNH, kKps>;
   constexpr int kStages = Cfg::kStages;
   constexpr uint32_t kIdesc = idesc_bf16_f32(Cfg::kMmaM, Cfg::kMmaN);
 
@@ -187,7 +191,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
           // SwiGLU: both CTAs use row nb*BNH (of the gate map / the up map);
           // GELU: CTA r loads rows nb*2*BNH + r*BNH of W.
           const int b_row = nb * p.b_row_stride + static_cast<int>(rank) * p.b1_row_offset;
-          for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          for (int kb = 0; kb < p.num_k_blocks; kb += kKps) {
             // The first pass over the ring needs no wait (every slot starts
             // empty), and skipping it saves the first wait on a barrier just
             // initialised (~0.4 us measured), which a one-k-block tile feels.
@@ -197,15 +201,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
               ok = false;
               break;
             }
-            const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
-            const uint32_t sb = sa + Cfg::kABytes;
+            const int nk = min(kKps, p.num_k_blocks - kb);
             const uint32_t fb_local = smem_u32(full_bar + stage);
-            if (leader) mbar_arrive_expect_tx(fb_local, 2 * Cfg::kStageBytes);
+            if (leader) mbar_arrive_expect_tx(fb_local, 2 * nk * Cfg::kKBlockBytes);
             const uint32_t fb = map_to_cta(fb_local, 0);
-            int ax, kx;
-            k_block_coords(p, kb, ax, kx);
-            tma_load_2d_pair(sa, &p.map_a, fb, ax, a_row);
-            tma_load_2d_pair(sb, map_b, fb, kx, b_row);
+            for (int j = 0; j < nk; ++j) {
+              const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes + j * Cfg::kKBlockBytes);
+              const uint32_t sb = sa + Cfg::kABytes;
+              int ax, kx;
+              k_block_coords(p, kb + j, ax, kx);
+              tma_load_2d_pair(sa, &p.map_a, fb, ax, a_row);
+              tma_load_2d_pair(sb, map_b, fb, kx, b_row);
+            }
             if (filled < kStages) ++filled;
             issued_mask |= 1u << stage;
             issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
@@ -252,20 +259,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
             const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
             int kb0, kb1;
             chunk_range<FLUSH>(p, c, kb0, kb1);
-            for (int kb = kb0; kb < kb1; ++kb) {
+            for (int kb = kb0; kb < kb1; kb += kKps) {
               if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
                 fail(kStatusMma);
                 ok = false;
                 break;
               }
               tc_fence_after();
-              const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes);
-              const uint32_t sb = sa + Cfg::kABytes;
+              const int nk = min(kKps, kb1 - kb);
+              for (int j = 0; j < nk; ++j) {
+                const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes + j * Cfg::kKBlockBytes);
+                const uint32_t sb = sa + Cfg::kABytes;
 #pragma unroll
-              for (int k = 0; k < kBlockK / 16; ++k) {
-                umma_bf16_pair(d_tmem, sdesc_kmajor_sw128(sa + k * 32),
-                               sdesc_kmajor_sw128(sb + k * 32), kIdesc,
-                               (kb != kb0 || k != 0) ? 1u : 0u);
+                for (int k = 0; k < kBlockK / 16; ++k) {
+                  umma_bf16_pair(d_tmem, sdesc_kmajor_sw128(sa + k * 32),
+                                 sdesc_kmajor_sw128(sb + k * 32), kIdesc,
+                                 (kb + j != kb0 || k != 0) ? 1u : 0u);
+                }
               }
               issued_any = true;
               umma_commit_pair_both(smem_u32(empty_bar + stage));
