@@ -734,7 +734,9 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
             const int nk = min(kKps, p.num_k_blocks - kb);
             const uint32_t fb = smem_u32(full_bar + stage);
             mbar_arrive_expect_tx(fb, nk * Cfg::kKBlockBytes);
-            for (int j = 0; j < nk; ++j) {
+#pragma unroll
+            for (int j = 0; j < kKps; ++j) {
+              if (j > 0 && j >= nk) break;  // k-block 0 of a stage always exists
               const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes + j * Cfg::kKBlockBytes);
               const uint32_t sb = sa + Cfg::kABytes;
               int ax, kx;
@@ -793,7 +795,9 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
               }
               tc_fence_after();
               const int nk = min(kKps, kb1 - kb);
-              for (int j = 0; j < nk; ++j) {
+#pragma unroll
+              for (int j = 0; j < kKps; ++j) {
+                if (j > 0 && j >= nk) break;  // k-block 0 of a stage always exists
                 const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes + j * Cfg::kKBlockBytes);
                 const uint32_t sb = sa + Cfg::kABytes;
 #pragma unroll

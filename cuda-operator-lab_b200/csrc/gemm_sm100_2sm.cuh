@@ -205,7 +205,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
             const uint32_t fb_local = smem_u32(full_bar + stage);
             if (leader) mbar_arrive_expect_tx(fb_local, 2 * nk * Cfg::kKBlockBytes);
             const uint32_t fb = map_to_cta(fb_local, 0);
-            for (int j = 0; j < nk; ++j) {
+#pragma unroll
+            for (int j = 0; j < kKps; ++j) {
+              if (j > 0 && j >= nk) break;  // k-block 0 of a stage always exists
               const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes + j * Cfg::kKBlockBytes);
               const uint32_t sb = sa + Cfg::kABytes;
               int ax, kx;
@@ -267,7 +269,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
               }
               tc_fence_after();
               const int nk = min(kKps, kb1 - kb);
-              for (int j = 0; j < nk; ++j) {
+#pragma unroll
+              for (int j = 0; j < kKps; ++j) {
+                if (j > 0 && j >= nk) break;  // k-block 0 of a stage always exists
                 const uint32_t sa = smem_u32(smem + stage * Cfg::kStageBytes + j * Cfg::kKBlockBytes);
                 const uint32_t sb = sa + Cfg::kABytes;
 #pragma unroll
