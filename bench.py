@@ -555,6 +555,8 @@ def run_ours(args, d: Dist) -> dict | None:
     torch.testing.assert_close(out_host[:4].float(), out[:4].cpu().float())
     del x_host, out_host, x_dev
 
+    gather = gather_variant(d, x, rstd, folded, out, args) if d.world > 1 and args.gather else None
+
     ops = op_table(d, pk) if not args.skip_ops else {}
 
     cpu = None
@@ -598,10 +600,62 @@ def run_ours(args, d: Dist) -> dict | None:
         "variants": {"rmsnorm_then_gemm": {
             "value": round(GEMM_FLOPS * args.steps / (unfold_ms / 1e3) / 1e12, 2),
             "ms_per_step": round(unfold_ms / args.steps, 4),
-            "step": "rmsnorm_bf16 (writes normalised X) + gemm_swiglu_bf16"}},
+            "step": "rmsnorm_bf16 (writes normalised X) + gemm_swiglu_bf16"},
+            **({"gathered_output": gather} if gather is not None else {})},
         "clocks": clock_info,
         "gpu_launches": 2 * args.steps,
         "ops": ops,
+    }
+
+
+def gather_variant(d: Dist, x, rstd, folded, out, args) -> dict:
+    """The headline step followed by the all-gather of the [M, N] output to
+    every rank, two ways: fused into the GEMM's epilogue (peer stores over
+    NVLink per finished tile, then the device flag barrier) and as the GEMM
+    followed by an NCCL all-gather.  Checks that both deliver the same blocks."""
+    from cuda_operator_lab import bindings as b
+    from cuda_operator_lab import sharding
+
+    n_local = N // d.world
+    pg = sharding.PeerColumnGather(M, N)
+    try:
+        def fused():
+            b.rmsnorm_rstd_bf16_into(x, rstd, EPS)
+            pg(x, folded, rstd)
+
+        fused_ms = time_region(d, fused, args.steps, args.warmup)
+        if b.peer_status(clear=True) != 0 or b.gemm_status(clear=True) != 0:
+            raise RuntimeError("peer barrier or GEMM bounded wait timed out in the gather step")
+        gathered = pg.outputs[(pg.calls - 1) % 2]
+        parts = torch.empty(d.world, M, n_local, device=x.device, dtype=torch.bfloat16)
+
+        def unfused():
+            b.rmsnorm_rstd_bf16_into(x, rstd, EPS)
+            b.gemm_swiglu_rowscale_bf16_into(x, rstd, folded, out)
+            d.dist.all_gather_into_tensor(parts, out)
+
+        unfused_ms = time_region(d, unfused, args.steps, args.warmup)
+        same = all(torch.equal(gathered[:, r * n_local:(r + 1) * n_local], parts[r])
+                   for r in range(d.world))
+        same = d.max(0.0 if same else 1.0) == 0.0
+        del gathered, parts
+    finally:
+        pg.close()
+    link_bytes = (d.world - 1) * M * n_local * 2  # sent by each rank
+    link_us = link_bytes / 770e3  # measured peer copy, GB/s per direction
+    gemm_us = GEMM_FLOPS / d.world / (peaks()["bf16_tflops_sustained"] * 1e6)
+    return {
+        "fused_ms_per_step": round(fused_ms / args.steps, 4),
+        "fused_value": round(GEMM_FLOPS * args.steps / (fused_ms / 1e3) / 1e12, 2),
+        "nccl_ms_per_step": round(unfused_ms / args.steps, 4),
+        "nccl_value": round(GEMM_FLOPS * args.steps / (unfused_ms / 1e3) / 1e12, 2),
+        "unit": "TFLOP/s",
+        "identical_blocks": same,
+        "nvlink_bytes_per_rank": link_bytes,
+        "bound_us": round(max(link_us, gemm_us), 1),
+        "bound": "nvlink" if link_us > gemm_us else "tensor",
+        "step": "rmsnorm_rstd + GEMM with gathering epilogue + peer flag barrier, vs "
+                "rmsnorm_rstd + GEMM + NCCL all_gather_into_tensor",
     }
 
 
@@ -791,6 +845,9 @@ def main() -> None:
     parser.add_argument("--cpu-seconds", type=float, default=15.0)
     parser.add_argument("--skip-ops", action="store_true")
     parser.add_argument("--skip-cpu", action="store_true")
+    parser.add_argument("--gather", action="store_true",
+                        help="N > 1: also time the step with the output all-gather, fused "
+                             "into the GEMM and with NCCL")
     parser.add_argument("--kernel-case", default=None,
                         help="run one op only (for profilers): NAME[:dims], see KERNEL_CASES")
     parser.add_argument("--reps", type=int, default=3)

@@ -15,6 +15,8 @@ COL_API const char* cuda_operator_error_string(int code) {
       return "the tensor-core GEMM needs a compute capability 10.x (sm_100) device";
     case col::kErrNoAllocCapacity:
       return "cuda_operator_lab_reduction_noalloc accepts at most 268435456 (2^28) elements";
+    case col::kErrGatherLayout:
+      return "the gathering GEMM needs k a multiple of 8 and 16-byte aligned x and weight";
     default:
       return cudaGetErrorString(static_cast<cudaError_t>(code));
   }

@@ -19,6 +19,7 @@ constexpr int kErrNoTensorMapEncoder = 10001;   // driver lacks cuTensorMapEncod
 constexpr int kErrTensorMapEncode = 10002;      // cuTensorMapEncodeTiled rejected a map
 constexpr int kErrDeviceNotSupported = 10003;   // device is not sm_100
 constexpr int kErrNoAllocCapacity = 10004;      // input larger than the allocation-free sum's scratch
+constexpr int kErrGatherLayout = 10005;         // peer-gather GEMM operands the tensor path cannot take
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -67,7 +67,7 @@ int encode_bf16_rows(CUtensorMap* map, const void* base, std::uint64_t rows, std
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>
 int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
-  using Cfg = TileCfg<BNH, FLUSH ? 1 : 2>;
+  using Cfg = TileCfg<BNH, FLUSH ? 1 : 2, col::sm100::epi_smem_reserve(EPI)>;
   auto kernel = col::sm100::gemm_bf16_tc_kernel<BNH, EPI, TOut, FLUSH>;
   static std::atomic<std::uint64_t> attr_set{0};
   const std::uint64_t bit = 1ull << (dev & 63);
@@ -89,7 +89,7 @@ int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
 // the answer).  Queried once per device; 0 if clusters are unavailable.
 template <int EPI, typename TOut>
 int max_pair_clusters(int dev) {
-  using Cfg = col::sm100::TileCfg2<128, 2>;
+  using Cfg = col::sm100::TileCfg2<128, 2, col::sm100::epi_smem_reserve(EPI)>;
   static int cached[64] = {};
   static std::once_flag flags[64];
   std::call_once(flags[dev & 63], [dev]() {
@@ -117,7 +117,7 @@ int max_pair_clusters(int dev) {
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>
 int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
-  using Cfg = col::sm100::TileCfg2<BNH, FLUSH ? 1 : 2>;
+  using Cfg = col::sm100::TileCfg2<BNH, FLUSH ? 1 : 2, col::sm100::epi_smem_reserve(EPI)>;
   auto kernel = col::sm100::gemm_bf16_tc2_kernel<BNH, EPI, TOut, FLUSH>;
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int grid = 2 * (tiles < clusters ? tiles : clusters);
@@ -128,7 +128,7 @@ int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>
 int set_smem_attr_2sm(int dev) {
-  using Cfg = col::sm100::TileCfg2<BNH, FLUSH ? 1 : 2>;
+  using Cfg = col::sm100::TileCfg2<BNH, FLUSH ? 1 : 2, col::sm100::epi_smem_reserve(EPI)>;
   static std::atomic<std::uint64_t> attr_set{0};
   const std::uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set.load(std::memory_order_acquire) & bit)) {
@@ -220,10 +220,19 @@ bool flush_wide_ok(bool pair) {
   return pair ? two : one;
 }
 
+// Output placement of the gathering epilogue: row stride `ld` (elements) and
+// the peer copies of the output block.
+struct GatherOut {
+  std::uint64_t ld;
+  int num_peers;
+  void* peers[col::sm100::kMaxPeers];
+};
+
 template <int EPI, typename TOut, bool FLUSH = false>
 int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, void* out,
                        std::uint64_t m, std::uint64_t n, cudaStream_t s,
-                       const void* residual = nullptr, const float* row_scale = nullptr) {
+                       const void* residual = nullptr, const float* row_scale = nullptr,
+                       const GatherOut* gather = nullptr) {
   int dev = 0;
   const col::DeviceInfo& info = col::device_info(&dev);
   if (info.cc_major != 10) return col::kErrDeviceNotSupported;
@@ -276,6 +285,15 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
   }
   p.out_ld = static_cast<int>(n);
   p.out_vec_ok = col::aligned16(out) && ((n * sizeof(TOut)) % 16 == 0);
+  if (gather != nullptr) {
+    p.out_ld = static_cast<int>(gather->ld);
+    p.out_vec_ok = col::aligned16(out) && ((gather->ld * sizeof(TOut)) % 16 == 0);
+    p.num_peers = gather->num_peers;
+    for (int i = 0; i < gather->num_peers; ++i) {
+      p.peer_out[i] = gather->peers[i];
+      p.out_vec_ok = p.out_vec_ok && col::aligned16(gather->peers[i]);
+    }
+  }
   p.flush_k_blocks = FLUSH ? kFlushKBlocks : 0;
   if constexpr (FLUSH) {
     if (use_pair) {
@@ -324,14 +342,15 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
 template <int EPI, typename TOut>
 int gemm_bf16_tc(const void* x, const void* w0, const void* w1, BMode mode, const float* bias,
                  void* out, std::uint64_t m, std::uint64_t n, std::uint64_t k, cudaStream_t s,
-                 const void* residual = nullptr, const float* row_scale = nullptr) {
+                 const void* residual = nullptr, const float* row_scale = nullptr,
+                 const GatherOut* gather = nullptr) {
   if ((k % 8) != 0 || !col::aligned16(x) || !col::aligned16(w0) ||
       (mode == BMode::kSwiGLU && !col::aligned16(w1))) {
     return -1;
   }
   TcOperands ops{x, k, w0, mode == BMode::kSwiGLU ? w1 : w0, n, k,
                  static_cast<int>((k + col::sm100::kBlockK - 1) / col::sm100::kBlockK), 0, 0u};
-  return launch_tensor_gemm<EPI, TOut>(ops, mode, bias, out, m, n, s, residual, row_scale);
+  return launch_tensor_gemm<EPI, TOut>(ops, mode, bias, out, m, n, s, residual, row_scale, gather);
 }
 
 // ---------------------------------------------------------------- fp32 on tensor cores
@@ -704,6 +723,42 @@ COL_API int cuda_operator_gemm_swiglu_rowscale_bf16(const void* input_bf16, cons
   if (rc != -1) return rc;
   return gemm_simt<__nv_bfloat16, col::sm100::kEpiSwiGLURowScale, __nv_bfloat16>(
       input_bf16, packed_weight_bf16, wu, nullptr, output_bf16, m, n, k, s, nullptr, row_scale);
+}
+
+// N-sharded packed GEMM + SwiGLU whose epilogue also all-gathers the output
+// over NVLink (no reference counterpart).  Rank r of g computes its [m, n]
+// column block (packed_weight_bf16 = its [2n, K] shard, row_scale as in
+// cuda_operator_gemm_swiglu_rowscale_bf16, or null for plain SwiGLU) and
+// stores it into each of the `num_dests` destinations: dests[0] is the
+// block's place in this GPU's [m, ld] output, dests[1..] the same place in the
+// other ranks' outputs, mapped into this process (cuda_operator_lab_peer_open).
+// The tensor-core path only: operands TMA cannot take (k not a multiple of 8,
+// unaligned x or weight) return 10005.
+COL_API int cuda_operator_gemm_swiglu_allgather_bf16(const void* input_bf16, const float* row_scale,
+                                                     const void* packed_weight_bf16,
+                                                     void* const* dests, int num_dests,
+                                                     uint64_t m, uint64_t k, uint64_t n,
+                                                     uint64_t ld, void* stream) {
+  if (m == 0 || n == 0) return 0;
+  if (!input_bf16 || !packed_weight_bf16 || !dests || num_dests < 1 ||
+      num_dests > col::sm100::kMaxPeers + 1 || ld < n || !dims_ok(m, n, k, 0x7fffffffull / 2) ||
+      ld > 0x7fffffffull) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
+  GatherOut g;
+  std::memset(&g, 0, sizeof(g));
+  g.ld = ld;
+  g.num_peers = num_dests - 1;
+  for (int i = 0; i < num_dests; ++i) {
+    if (dests[i] == nullptr) return static_cast<int>(cudaErrorInvalidValue);
+    if (i > 0) g.peers[i - 1] = dests[i];
+  }
+  const cudaStream_t s = col::as_stream(stream);
+  const void* wu = up_half(packed_weight_bf16, n, k, 2);
+  const int rc = gemm_bf16_tc<col::sm100::kEpiSwiGLUGather, __nv_bfloat16>(
+      input_bf16, packed_weight_bf16, wu, BMode::kSwiGLU, nullptr, dests[0], m, n, k, s, nullptr,
+      row_scale, &g);
+  return rc == -1 ? col::kErrGatherLayout : rc;
 }
 
 COL_API int cuda_operator_lab_gemm_status(unsigned int* status, int clear) {

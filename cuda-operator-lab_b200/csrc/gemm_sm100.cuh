@@ -42,7 +42,12 @@ enum Epilogue : int {
   kEpiBiasGeluTanh = 3,     // out = gelu_tanh(acc + bias[n])
   kEpiResidual = 4,         // out = acc + residual[m, n] (bf16 residual, down projection)
   kEpiSwiGLURowScale = 5,   // g, u scaled by row_scale[m] first (RMSNorm folded into the GEMM)
+  kEpiSwiGLUGather = 6,     // as kEpiSwiGLURowScale (no scale when row_scale is null); every
+                            // output row run is also stored to each peer_out (column all-gather)
 };
+
+// Peer destinations of the gathering epilogue (an 8-GPU NVLink domain).
+constexpr int kMaxPeers = 7;
 
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;  // bf16 elements per k-block: one 128-byte swizzle row
@@ -50,6 +55,14 @@ constexpr int kGroupM = 16;  // m-blocks per rasterisation group (L2 reuse of B)
 constexpr int kEpiWarps = 8;       // warps 4..11: two per TMEM lane quarter
 constexpr int kEpiGroups = kEpiWarps / 4;
 constexpr int kCtaThreads = 128 + 32 * kEpiWarps;  // producer, MMA, TMEM, idle + epilogue
+// The gathering epilogue stages each warp's 32 rows x up to 64 output columns
+// (bf16, 128 bytes a row) in shared memory so that its stores to other GPUs
+// go out as whole 128-byte row runs.
+constexpr uint32_t kGatherRowBytes = 128;
+constexpr uint32_t kGatherWarpBytes = 32 * kGatherRowBytes;
+constexpr uint32_t epi_smem_reserve(int epi) {
+  return epi == kEpiSwiGLUGather ? kEpiWarps * kGatherWarpBytes : 0u;
+}
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 // Status bits written on a bounded-wait timeout.
@@ -84,6 +97,10 @@ struct __align__(64) GemmParams {
   int seg_k_blocks;
   uint32_t seg_pairs;
   int flush_k_blocks;  // fp32 emulation: k-blocks per flushed chunk of segment 0
+  // kEpiSwiGLUGather: the same [m, n] block (row stride out_ld) in the output
+  // buffers of other GPUs, mapped into this process (peer stores over NVLink).
+  int num_peers;
+  void* peer_out[kMaxPeers];
 };
 
 // Column (x) coordinates of k-block kb in A and in B.
@@ -150,7 +167,9 @@ __host__ __device__ constexpr uint32_t pow2_at_least(uint32_t v) {
 // (barrier wait, commit) costs ~0.13 us that does not overlap the MMAs
 // (measured), so stages of two k-blocks halve it per k-block; the FLUSH
 // kernels keep one k-block per stage (their chunk boundaries).
-template <int BNH, int KPS = 1>
+// RESERVE = shared memory the epilogue keeps for itself (the gathering
+// epilogue's staging tiles), taken from the ring.
+template <int BNH, int KPS = 1, uint32_t RESERVE = 0>
 struct TileCfg {
   static_assert(BNH % 16 == 0 && BNH >= 32 && BNH <= 128, "unsupported B box height");
   static_assert(KPS == 1 || KPS == 2, "one or two k-blocks per stage");
@@ -160,11 +179,13 @@ struct TileCfg {
   static constexpr uint32_t kKBlockBytes = kABytes + kBBytes;  // [A | B] of one k-block
   static constexpr uint32_t kStageBytes = KPS * kKBlockBytes;
   static constexpr uint32_t kBarrierBytes = 256;
-  static constexpr int kStagesFit = static_cast<int>((kSmemLimit - 1024 - kBarrierBytes) / kStageBytes);
+  static constexpr int kStagesFit =
+      static_cast<int>((kSmemLimit - 1024 - kBarrierBytes - RESERVE) / kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr uint32_t kAccStride = pow2_at_least(kMmaN);  // TMEM columns per accumulator
   static constexpr uint32_t kTmemCols = 2 * kAccStride;
-  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+  static constexpr uint32_t kEpiSmemOffset = kStages * kStageBytes + kBarrierBytes;
+  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + RESERVE;
   static_assert(kTmemCols <= 512, "two accumulators must fit in TMEM");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
 };
@@ -570,6 +591,100 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, int row, int 
   }
 }
 
+// ------------------------------------------------------------ gathering epilogue
+//
+// kEpiSwiGLUGather: the two warps of a TMEM lane quarter split a tile's BNH
+// output columns into contiguous parts (group 0 the first ceil(BNH/32)
+// 16-column chunks, group 1 the rest; at most 64 columns).  A warp computes
+// its part of its 32 rows, stores it to this GPU's output and into its
+// staging tile (row r at r * 128 bytes, 16-byte segment s in slot s ^ (r & 7),
+// so neither the row-wise writes nor the segment-wise reads conflict on
+// banks), releases the accumulator, and then sends the staging tile to every
+// peer output with 8 lanes per row: one store instruction moves four whole
+// 128-byte row runs over NVLink instead of 32 separate 16-byte pieces.
+
+template <int BNH>
+struct GatherSplit {
+  static constexpr int kChunks = BNH / 16;
+  static constexpr int kChunks0 = (kChunks + 1) / 2;
+  static_assert(kChunks0 * 16 * 2 <= static_cast<int>(kGatherRowBytes), "staging row too short");
+  __device__ __forceinline__ static int first(int group) { return group == 0 ? 0 : kChunks0; }
+  __device__ __forceinline__ static int last(int group) { return group == 0 ? kChunks0 : kChunks; }
+};
+
+template <int BNH>
+__device__ __forceinline__ void epilogue_gather_local(const GemmParams& p, int row, int nb,
+                                                      uint32_t t_row, int group, int lane,
+                                                      uint8_t* stage) {
+  using Split = GatherSplit<BNH>;
+  const int c0 = Split::first(group);
+  const int c1 = Split::last(group);
+  const int col_base = nb * BNH;
+  float rs = 1.0f;
+  if (p.row_scale != nullptr) rs = row < p.m ? __ldg(p.row_scale + row) : 0.0f;
+  uint8_t* my_row = stage + lane * kGatherRowBytes;
+#pragma unroll 1
+  for (int ci = c0; ci < c1; ++ci) {
+    const int c = ci * 16;
+    uint32_t g[16], u[16];
+    tmem_ld16x2(t_row + c, t_row + BNH + c, g, u);
+    float o[16], lo[8], hi[8];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      // rs = 1 multiplies exactly: the same bits as the unscaled epilogue
+      o[j] = silu_fast(__uint_as_float(g[j]) * rs) * (__uint_as_float(u[j]) * rs);
+    }
+    store_chunk<__nv_bfloat16, 16>(p, row, col_base + c, o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      lo[j] = o[j];
+      hi[j] = o[8 + j];
+    }
+    const int seg = 2 * (ci - c0);
+    *reinterpret_cast<uint4*>(my_row + ((seg ^ (lane & 7)) << 4)) = pack_bf16x8(lo);
+    *reinterpret_cast<uint4*>(my_row + (((seg + 1) ^ (lane & 7)) << 4)) = pack_bf16x8(hi);
+  }
+}
+
+// Sends a warp's staging tile (rows row0.., its column part of n-block nb)
+// to every peer output.  Call after __syncwarp() following the local part.
+template <int BNH>
+__device__ __forceinline__ void epilogue_gather_peers(const GemmParams& p, int row0, int nb,
+                                                      int group, int lane, const uint8_t* stage) {
+  using Split = GatherSplit<BNH>;
+  if (p.num_peers == 0) return;
+  const int c0 = Split::first(group);
+  const int segs = 2 * (Split::last(group) - c0);
+  const int col0 = nb * BNH + c0 * 16;
+#pragma unroll 1
+  for (int idx = lane; idx < 32 * segs; idx += 32) {
+    const int r = idx / segs;
+    const int sg = idx - r * segs;
+    const int grow = row0 + r;
+    const int gcol = col0 + sg * 8;
+    if (grow >= p.m || gcol >= p.n) continue;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + r * kGatherRowBytes + ((sg ^ (r & 7)) << 4));
+    const std::size_t off = static_cast<std::size_t>(grow) * p.out_ld + gcol;
+    if (p.out_vec_ok && gcol + 8 <= p.n) {
+#pragma unroll 1
+      for (int i = 0; i < p.num_peers; ++i) {
+        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.peer_out[i]) + off) = v;
+      }
+    } else {
+      float f[8];
+      unpack_bf16x8(v, f);
+#pragma unroll 1
+      for (int i = 0; i < p.num_peers; ++i) {
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.peer_out[i]) + off;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (gcol + j < p.n) dst[j] = __float2bfloat16_rn(f[j]);
+        }
+      }
+    }
+  }
+}
+
 // Register sums for FLUSH: this thread's columns of one accumulator row.
 // Slot i covers accumulator columns c = group*16 + i*32 (16 wide; SwiGLU adds
 // the up columns BNH + c), so a thread holds BNH floats.
@@ -647,7 +762,8 @@ __device__ __forceinline__ void epilogue_sums(const GemmParams& p, int row, int 
 template <int BNH, int EPI, typename TOut, bool FLUSH = false>
 __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __grid_constant__ GemmParams p) {
   constexpr int kKps = FLUSH ? 1 : 2;
-  using Cfg = TileCfg<BNH, kKps>;
+  using Cfg = TileCfg<BNH, kKps, epi_smem_reserve(EPI)>;
+  static_assert(EPI != kEpiSwiGLUGather || (sizeof(TOut) == 2 && !FLUSH), "gather: bf16 out");
   constexpr int kStages = Cfg::kStages;
   constexpr uint32_t kIdesc = idesc_bf16_f32(kBlockM, Cfg::kMmaN);
 
@@ -831,6 +947,8 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
     const int q = warp & 3;
     const int group = (warp - 4) >> 2;
     const int chunks = tile_chunks<FLUSH>(p);
+    uint8_t* gather_stage = smem + Cfg::kEpiSmemOffset + (warp - 4) * kGatherWarpBytes;
+    (void)gather_stage;
     int local = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
@@ -852,6 +970,8 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccStride;
         if constexpr (FLUSH) {
           accumulate_chunk<BNH, EPI>(t_row, group, c == 0, sums);
+        } else if constexpr (EPI == kEpiSwiGLUGather) {
+          epilogue_gather_local<BNH>(p, row, nb, t_row, group, lane, gather_stage);
         } else {
           epilogue_tile<BNH, EPI, TOut>(p, row, nb, t_row, group);
         }
@@ -862,7 +982,16 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
       if constexpr (FLUSH) {
         if (ok) epilogue_sums<BNH, EPI, TOut>(p, row, nb, group, sums);
       }
+      if constexpr (EPI == kEpiSwiGLUGather) {
+        // the accumulator is already released: the next tile's MMAs run
+        // while this tile travels to the peers
+        if (ok) epilogue_gather_peers<BNH>(p, row - lane, nb, group, lane, gather_stage);
+        __syncwarp();
+      }
     }
+    // Peer stores of this thread complete before the kernel does, so a flag
+    // raised after the launch (stream order) publishes them system-wide.
+    if constexpr (EPI == kEpiSwiGLUGather) __threadfence_system();
   }
 
   tc_fence_before();

@@ -26,7 +26,7 @@ namespace col {
 namespace sm100 {
 
 // KPS = k-blocks per pipeline stage, as in TileCfg.
-template <int BNH, int KPS = 1>
+template <int BNH, int KPS = 1, uint32_t RESERVE = 0>
 struct TileCfg2 {
   static_assert(BNH % 16 == 0 && BNH >= 32 && BNH <= 128, "unsupported B box height");
   static_assert(KPS == 1 || KPS == 2, "one or two k-blocks per stage");
@@ -37,11 +37,13 @@ struct TileCfg2 {
   static constexpr uint32_t kKBlockBytes = kABytes + kBBytes;  // [A | B] of one k-block
   static constexpr uint32_t kStageBytes = KPS * kKBlockBytes;
   static constexpr uint32_t kBarrierBytes = 256;
-  static constexpr int kStagesFit = static_cast<int>((kSmemLimit - 1024 - kBarrierBytes) / kStageBytes);
+  static constexpr int kStagesFit =
+      static_cast<int>((kSmemLimit - 1024 - kBarrierBytes - RESERVE) / kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr uint32_t kAccStride = pow2_at_least(kMmaN);
   static constexpr uint32_t kTmemCols = 2 * kAccStride;
-  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes;
+  static constexpr uint32_t kEpiSmemOffset = kStages * kStageBytes + kBarrierBytes;
+  static constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024 + kBarrierBytes + RESERVE;
   static_assert(kTmemCols <= 512, "two accumulators must fit in TMEM");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
 };
@@ -122,7 +124,8 @@ template <int BNH, int EPI, typename TOut, bool FLUSH = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ GemmParams p) {
   constexpr int kKps = FLUSH ? 1 : 2;
-  using Cfg = TileCfg2<BNH, kKps>;
+  using Cfg = TileCfg2<BNH, kKps, epi_smem_reserve(EPI)>;
+  static_assert(EPI != kEpiSwiGLUGather || (sizeof(TOut) == 2 && !FLUSH), "gather: bf16 out");
   constexpr int kStages = Cfg::kStages;
   constexpr uint32_t kIdesc = idesc_bf16_f32(Cfg::kMmaM, Cfg::kMmaN);
 
@@ -304,6 +307,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
     const int q = warp & 3;
     const int group = (warp - 4) >> 2;
     const int chunks = tile_chunks<FLUSH>(p);
+    uint8_t* gather_stage = smem + Cfg::kEpiSmemOffset + (warp - 4) * kGatherWarpBytes;
+    (void)gather_stage;
     int local = 0;
     bool ok = true;
     for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
@@ -323,6 +328,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccStride;
         if constexpr (FLUSH) {
           accumulate_chunk<BNH, EPI>(t_row, group, c == 0, sums);
+        } else if constexpr (EPI == kEpiSwiGLUGather) {
+          epilogue_gather_local<BNH>(p, row, nb, t_row, group, lane, gather_stage);
         } else {
           epilogue_tile<BNH, EPI, TOut>(p, row, nb, t_row, group);
         }
@@ -333,7 +340,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
       if constexpr (FLUSH) {
         if (ok) epilogue_sums<BNH, EPI, TOut>(p, row, nb, group, sums);
       }
+      if constexpr (EPI == kEpiSwiGLUGather) {
+        // the accumulator is already released: the next tile's MMAs run
+        // while this tile travels to the peers
+        if (ok) epilogue_gather_peers<BNH>(p, row - lane, nb, group, lane, gather_stage);
+        __syncwarp();
+      }
     }
+    // Peer stores of this thread complete before the kernel does, so a flag
+    // raised after the launch (stream order) publishes them system-wide.
+    if constexpr (EPI == kEpiSwiGLUGather) __threadfence_system();
   }
 
   // Neither CTA leaves while the other may still address its shared memory.

@@ -17,7 +17,8 @@ There is no fallback: if the shared library is missing, the first call raises
 Functions after the reference set (``rmsnorm_bf16``, ``fused_residual_layernorm_h``,
 ``fused_residual_rmsnorm``, ``gemm_swiglu_bf16``, ``gemm_bias_gelu_bf16``,
 ``gemm_residual_bf16``, ``rmsnorm_rstd_bf16``, ``gemm_swiglu_rowscale_bf16``,
-``reduction_partial_f64``) expose the library's additional entry points.
+``gemm_swiglu_allgather_bf16``, ``reduction_partial_f64``, ``peer_*``) expose the
+library's additional entry points.
 """
 
 from __future__ import annotations
@@ -25,7 +26,7 @@ from __future__ import annotations
 import ctypes
 import os
 from pathlib import Path
-from typing import Callable
+from typing import Callable, Sequence
 
 import torch
 
@@ -74,7 +75,16 @@ _SIGNATURES["cuda_operator_gemm_bias_gelu_bf16"] = [_P, _P, _P, _P, _U64, _U64, 
 _SIGNATURES["cuda_operator_gemm_residual_bf16"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
 _SIGNATURES["cuda_operator_rmsnorm_rstd_bf16"] = [_P, _P, _U64, _U64, _F32, _P]
 _SIGNATURES["cuda_operator_gemm_swiglu_rowscale_bf16"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
+_SIGNATURES["cuda_operator_gemm_swiglu_allgather_bf16"] = [
+    _P, _P, _P, _P, _I32, _U64, _U64, _U64, _U64, _P]
 _SIGNATURES["cuda_operator_reduction_partial_f64"] = [_P, _P, _U64, _P]
+_SIGNATURES["cuda_operator_lab_peer_handle_bytes"] = []
+_SIGNATURES["cuda_operator_lab_peer_alloc"] = [_U64, _P, _P]
+_SIGNATURES["cuda_operator_lab_peer_open"] = [_P, _P]
+_SIGNATURES["cuda_operator_lab_peer_close"] = [_P]
+_SIGNATURES["cuda_operator_lab_peer_free"] = [_P]
+_SIGNATURES["cuda_operator_lab_peer_barrier"] = [_P, _I32, _I32, ctypes.c_uint32, _U64, _P]
+_SIGNATURES["cuda_operator_lab_peer_status"] = [_P, _I32]
 _SIGNATURES["cuda_operator_lab_device_info"] = [_P, _P, _P]
 _SIGNATURES["cuda_operator_lab_build_tag"] = []
 _SIGNATURES["cuda_operator_lab_gemm_status"] = [_P, _I32]
@@ -82,6 +92,7 @@ _SIGNATURES["cuda_operator_lab_reduction_noalloc"] = [_P, _P, _U64, _P]
 
 _RESTYPES = {
     "cuda_operator_error_string": ctypes.c_char_p,
+    "cuda_operator_lab_peer_handle_bytes": ctypes.c_uint64,
     "cuda_operator_lab_build_tag": ctypes.c_char_p,
 }
 
@@ -825,6 +836,105 @@ def gemm_swiglu_rowscale_bf16(x_bf16: torch.Tensor, row_scale: torch.Tensor,
 
 __all__ += ["rmsnorm_rstd_bf16_into", "rmsnorm_rstd_bf16", "fold_rmsnorm_weight",
             "gemm_swiglu_rowscale_bf16_into", "gemm_swiglu_rowscale_bf16"]
+
+# ---------------------------------------------------------------- GEMM + SwiGLU + all-gather
+# no reference counterpart: the N-sharded GEMM whose epilogue also stores its
+# output block into the other ranks' outputs (peer memory over NVLink)
+
+
+def gemm_swiglu_allgather_bf16(x_bf16: torch.Tensor, row_scale: torch.Tensor | None,
+                               packed_weight_bf16: torch.Tensor, dests: Sequence[int],
+                               ld: int) -> None:
+    """bf16(silu(rs * g) * (rs * u)) of this rank's packed weight shard [2n, K]
+    (rs = row_scale[row], or 1 when row_scale is None), stored to every address in
+    ``dests``: each is the origin of this rank's [M, n] column block inside an
+    [M, ld] bf16 output -- this GPU's own first, then the other ranks' as mapped by
+    :func:`peer_open`.  Enqueued on the current stream of x's device; follow it
+    with :func:`peer_barrier` before reading blocks other ranks wrote."""
+    tensors = [x_bf16, packed_weight_bf16] + ([row_scale] if row_scale is not None else [])
+    if not all(t.is_cuda for t in tensors):
+        raise ValueError("GEMM SwiGLU tensors must be CUDA tensors")
+    if x_bf16.ndim != 2 or packed_weight_bf16.ndim != 2:
+        raise ValueError("x and packed weight must be 2-D")
+    if x_bf16.shape[1] != packed_weight_bf16.shape[1] or packed_weight_bf16.shape[0] % 2:
+        raise ValueError("packed weight must be [2N, K] with K = x.shape[1]")
+    if x_bf16.dtype != torch.bfloat16 or packed_weight_bf16.dtype != torch.bfloat16:
+        raise TypeError("GEMM SwiGLU all-gather expects bfloat16 x and weight")
+    if not all(t.is_contiguous() for t in tensors):
+        raise ValueError("all GEMM SwiGLU tensors must be contiguous")
+    n = packed_weight_bf16.shape[0] // 2
+    m, k = x_bf16.shape
+    if row_scale is not None and (row_scale.shape != (m,) or row_scale.dtype != torch.float32):
+        raise ValueError("row_scale must be a float32 vector of length M")
+    if not 1 <= len(dests) <= 8 or any(int(d) == 0 for d in dests):
+        raise ValueError("dests must hold 1 to 8 non-null device addresses")
+    if ld < n:
+        raise ValueError("ld must be at least the block width n")
+    if m == 0 or n == 0:
+        return
+    array = (ctypes.c_void_p * len(dests))(*[int(d) for d in dests])
+    _call("cuda_operator_gemm_swiglu_allgather_bf16", _ptr(x_bf16),
+          _ptr(row_scale) if row_scale is not None else ctypes.c_void_p(),
+          _ptr(packed_weight_bf16), array, ctypes.c_int(len(dests)), ctypes.c_uint64(m),
+          ctypes.c_uint64(k), ctypes.c_uint64(n), ctypes.c_uint64(ld), _stream(x_bf16))
+
+
+def peer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """Zero-filled device allocation on the current device that other processes
+    can map: (address, handle bytes to send them)."""
+    library = _library()
+    size = int(library.handle.cuda_operator_lab_peer_handle_bytes())
+    handle = ctypes.create_string_buffer(size)
+    addr = ctypes.c_void_p()
+    library.check(library.handle.cuda_operator_lab_peer_alloc(
+        ctypes.c_uint64(nbytes), ctypes.byref(addr), handle))
+    return int(addr.value), handle.raw
+
+
+def peer_open(handle: bytes) -> int:
+    """Address of another process's :func:`peer_alloc` allocation in this process."""
+    addr = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(bytes(handle), len(handle))
+    _call("cuda_operator_lab_peer_open", buf, ctypes.byref(addr))
+    return int(addr.value)
+
+
+def peer_close(addr: int) -> None:
+    """Unmaps an address returned by :func:`peer_open`."""
+    _call("cuda_operator_lab_peer_close", ctypes.c_void_p(addr))
+
+
+def peer_free(addr: int) -> None:
+    """Frees a :func:`peer_alloc` allocation (after every peer closed its mapping)."""
+    _call("cuda_operator_lab_peer_free", ctypes.c_void_p(addr))
+
+
+def peer_barrier(flag_addrs: Sequence[int], rank: int, epoch: int,
+                 timeout_ns: int = 5_000_000_000, stream: torch.cuda.Stream | None = None) -> None:
+    """Enqueues the device-side barrier of len(flag_addrs) ranks at ``epoch`` on
+    ``stream`` (default: the current stream).  flag_addrs[j] is rank j's
+    zero-initialised uint32 flag array as mapped here; epochs increase per call.  A
+    wait longer than timeout_ns sets the :func:`peer_status` bit instead of hanging."""
+    world = len(flag_addrs)
+    if not 1 <= world <= 8 or not 0 <= rank < world:
+        raise ValueError("need 1 <= world <= 8 and 0 <= rank < world")
+    array = (ctypes.c_void_p * world)(*[int(a) for a in flag_addrs])
+    s = stream if stream is not None else torch.cuda.current_stream()
+    _call("cuda_operator_lab_peer_barrier", array, ctypes.c_int(rank), ctypes.c_int(world),
+          ctypes.c_uint32(epoch & 0xFFFFFFFF), ctypes.c_uint64(timeout_ns),
+          ctypes.c_void_p(s.cuda_stream))
+
+
+def peer_status(clear: bool = True) -> int:
+    """Peer status word of the current device (bit 1: a barrier wait timed out).
+    Synchronises the device."""
+    value = ctypes.c_uint(0)
+    _call("cuda_operator_lab_peer_status", ctypes.byref(value), ctypes.c_int(1 if clear else 0))
+    return int(value.value)
+
+
+__all__ += ["gemm_swiglu_allgather_bf16", "peer_alloc", "peer_open", "peer_close", "peer_free",
+            "peer_barrier", "peer_status"]
 
 # ---------------------------------------------------------------- GEMM + SwiGLU
 # reference bindings.py:2036-2818

@@ -10,7 +10,11 @@ The reference is single-GPU; these helpers add the BASELINE sharding plan:
   first), and X is replicated; the optional output gather is a column-block
   all-gather;
 * the global sum reduces each rank's chunk to an fp64 partial and
-  all-reduces the partials (the only collective on the data path).
+  all-reduces the partials (the only collective on the data path);
+* :class:`PeerColumnGather` fuses the optional output gather into the GEMM:
+  each rank's epilogue stores its column block straight into every rank's
+  [M, N] output over NVLink (CUDA IPC peer mappings), then a device-side flag
+  barrier tells each rank that the other blocks have landed.
 
 Collectives go through ``torch.distributed`` (NCCL on GPUs, gloo on CPU for
 tests of this host logic).  Per-rank compute is injectable so the partition
@@ -19,7 +23,7 @@ and combine logic is testable on CPU ranks.
 
 from __future__ import annotations
 
-from typing import Callable
+from typing import Callable, Sequence
 
 import torch
 import torch.distributed as dist
@@ -98,3 +102,152 @@ def mlp_block_sharded(x: torch.Tensor, norm_weight: torch.Tensor, packed_shard: 
         out = torch.empty((x.shape[0], packed_shard.shape[0] // 2), device=x.device,
                           dtype=torch.bfloat16)
     return bindings.gemm_swiglu_bf16_into(xn, packed_shard, out)
+
+
+# ---------------------------------------------------------------- fused output gather
+
+_FLAG_BYTES = 256  # one uint32 per rank (up to 8), padded
+
+
+class _CudaWords:
+    """__cuda_array_interface__ view of raw device memory as int16 words."""
+
+    def __init__(self, addr: int, shape: tuple[int, ...]) -> None:
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<i2", "data": (addr, False),
+                                         "version": 3, "strides": None}
+
+
+class LibraryPeers:
+    """Peer memory, fused gather GEMM and barrier of the CUDA library.
+
+    The operations :class:`PeerColumnGather` needs, as one object so that a
+    test can substitute host-side stand-ins for them."""
+
+    def __init__(self, timeout_ns: int = 5_000_000_000) -> None:
+        from . import bindings
+
+        self._b = bindings
+        self.timeout_ns = timeout_ns
+
+    def alloc(self, nbytes: int) -> tuple[int, bytes]:
+        return self._b.peer_alloc(nbytes)
+
+    def open(self, handle: bytes) -> int:
+        return self._b.peer_open(handle)
+
+    def close(self, addr: int) -> None:
+        self._b.peer_close(addr)
+
+    def free(self, addr: int) -> None:
+        self._b.peer_free(addr)
+
+    def view(self, addr: int, m: int, n: int) -> torch.Tensor:
+        return torch.as_tensor(_CudaWords(addr, (m, n)), device="cuda").view(torch.bfloat16)
+
+    def gemm(self, x: torch.Tensor, row_scale: torch.Tensor | None, packed_shard: torch.Tensor,
+             dests: Sequence[int], ld: int) -> None:
+        self._b.gemm_swiglu_allgather_bf16(x, row_scale, packed_shard, dests, ld)
+
+    def barrier(self, flag_addrs: Sequence[int], rank: int, epoch: int) -> None:
+        self._b.peer_barrier(flag_addrs, rank, epoch, self.timeout_ns)
+
+    def status(self) -> int:
+        return self._b.peer_status(clear=True)
+
+
+class PeerColumnGather:
+    """N-sharded GEMM+SwiGLU with its column all-gather fused into the GEMM.
+
+    Every rank holds two [M, N] bf16 output buffers in memory the other ranks
+    have mapped (CUDA IPC), plus a flag array.  A call runs the rank's GEMM
+    with the gathering epilogue -- each finished tile of its [M, N/g] column
+    block is stored into the same place of every rank's current buffer, the
+    NVLink transfers overlapping the remaining tiles -- and then the device
+    barrier, after which the returned buffer holds all g blocks.  Everything
+    is stream-ordered on the current stream; the host never waits.
+
+    The two buffers alternate.  A returned output stays valid until the call
+    after the next one, provided each rank reads it on the current stream
+    before its own next call: rank r's GEMM of call c + 2 runs after r passed
+    barrier c + 1, which every other rank p entered only after its GEMM
+    c + 1, and so after p's reads of the output of call c.
+
+    Construction and :meth:`close` are collective (``torch.distributed``
+    object all-gather and barriers on ``group``).  ``peers`` supplies the
+    memory, GEMM and barrier operations (default: the CUDA library).
+    """
+
+    def __init__(self, m: int, n: int, group=None, peers=None) -> None:
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if not 1 <= self.world <= 8:
+            raise ValueError("the fused gather supports 1 to 8 ranks")
+        if n % self.world:
+            raise ValueError("N must divide evenly between the ranks")
+        self.m, self.n, self.n_local = m, n, n // self.world
+        self.group = group
+        self.peers = peers if peers is not None else LibraryPeers()
+        out_bytes = m * n * 2
+        self._flag_offset = -(-out_bytes // 256) * 256
+        nbytes = self._flag_offset + _FLAG_BYTES
+        local = [self.peers.alloc(nbytes) for _ in range(2)]
+        self._local = [addr for addr, _ in local]
+        handles = [h for _, h in local]
+        every = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(every, handles, group=group)
+        else:
+            every = [handles]
+        # addrs[i][j]: rank j's buffer i as mapped here
+        self._opened: list[int] = []
+        self.addrs = [[0] * self.world for _ in range(2)]
+        for j in range(self.world):
+            for i in range(2):
+                if j == self.rank:
+                    self.addrs[i][j] = self._local[i]
+                else:
+                    self.addrs[i][j] = self.peers.open(every[j][i])
+                    self._opened.append(self.addrs[i][j])
+        self.outputs = [self.peers.view(self._local[i], m, n) for i in range(2)]
+        self.flag_addrs = [self.addrs[0][j] + self._flag_offset for j in range(self.world)]
+        self.calls = 0
+        if self.world > 1:
+            dist.barrier(group=group)  # every mapping exists before any peer store
+
+    def destinations(self, call: int) -> list[int]:
+        """Addresses the gathering epilogue of `call` stores to: this rank's
+        block in its own buffer first, then in rank+1, rank+2, ... (mod g)."""
+        i = call % 2
+        offset = self.rank * self.n_local * 2
+        order = [(self.rank + j) % self.world for j in range(self.world)]
+        return [self.addrs[i][r] + offset for r in order]
+
+    def __call__(self, x: torch.Tensor, packed_shard: torch.Tensor,
+                 row_scale: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's GEMM (packed_shard [2N/g, K], optional row scale) and the
+        gather; returns the [M, N] output holding every rank's block."""
+        if x.shape[0] != self.m or packed_shard.shape[0] != 2 * self.n_local:
+            raise ValueError(f"expected x[{self.m}, K] and a packed shard of "
+                             f"{2 * self.n_local} rows")
+        call = self.calls
+        self.calls += 1
+        self.peers.gemm(x, row_scale, packed_shard, self.destinations(call), self.n)
+        self.peers.barrier(self.flag_addrs, self.rank, self.calls)
+        return self.outputs[call % 2]
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (collective)."""
+        if self._local is None:
+            return
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no rank still stores into a buffer
+        for addr in self._opened:
+            self.peers.close(addr)
+        if self.world > 1:
+            dist.barrier(group=self.group)  # every mapping closed before the frees
+        self.outputs = []
+        for addr in self._local:
+            self.peers.free(addr)
+        self._local = None

@@ -197,6 +197,50 @@ int cuda_operator_gemm_bias_gelu_bf16(const void* input_bf16, const void* weight
  * succeeds; NULL, k == 0 or sizes above INT32_MAX return cudaErrorInvalidValue. */
 int cuda_operator_gemm_residual_bf16(const void* input_bf16, const void* weight_bf16, const void* residual_bf16, void* output_bf16, uint64_t m, uint64_t k, uint64_t n, void* stream);
 
+/* N-sharded packed GEMM + SwiGLU with the output all-gather fused into its
+ * epilogue (no reference counterpart; the column gather after the N-sharded
+ * cuda_operator_gemm_swiglu_bf16 / _rowscale_bf16).  Rank r of g computes its
+ * [m, n] output column block from x[m, k] and its packed weight shard [2n, k]
+ * (g, u scaled by row_scale[m] first when row_scale is not NULL) and stores it
+ * to each of the num_dests (1..8) destinations: dests (a HOST array of device
+ * addresses) holds the block's origin in this GPU's [m, ld] bf16 output
+ * first, then the same origin in the other ranks' outputs as mapped by
+ * cuda_operator_lab_peer_open.  The stores to other GPUs travel over NVLink
+ * while later tiles compute.  Follow it with cuda_operator_lab_peer_barrier on
+ * the same stream before reading blocks written by other ranks.  Tensor-core
+ * path only: k not a multiple of 8 or unaligned x / weight return 10005; NULL
+ * pointers, num_dests outside 1..8 or ld < n return cudaErrorInvalidValue;
+ * m == 0 or n == 0 succeeds. */
+int cuda_operator_gemm_swiglu_allgather_bf16(const void* input_bf16, const float* row_scale, const void* packed_weight_bf16, void* const* dests, int num_dests, uint64_t m, uint64_t k, uint64_t n, uint64_t ld, void* stream);
+
+/* Peer memory for the gathering GEMM, shared by the processes of one node
+ * (one per GPU) through CUDA IPC.  peer_alloc: zero-filled device allocation
+ * of `bytes` on the current device; *ptr = its address, `handle` receives
+ * cuda_operator_lab_peer_handle_bytes() opaque bytes to send to the other
+ * processes.  peer_open: maps such a handle from another process (address
+ * usable by kernels on the current device).  peer_close undoes peer_open;
+ * peer_free releases a peer_alloc allocation after every mapping of it is
+ * closed.  No reference counterpart. */
+uint64_t cuda_operator_lab_peer_handle_bytes(void);
+int cuda_operator_lab_peer_alloc(uint64_t bytes, void** ptr, void* handle);
+int cuda_operator_lab_peer_open(const void* handle, void** ptr);
+int cuda_operator_lab_peer_close(void* ptr);
+int cuda_operator_lab_peer_free(void* ptr);
+
+/* Device-side barrier of `world` (1..8) ranks at `epoch`, enqueued on
+ * `stream`: flag_arrays (a HOST array) holds each rank's uint32[world] flag
+ * array, zero-initialised, as mapped in this process.  Each rank writes epoch
+ * into its slot of every array, then waits for every slot of its own array to
+ * reach epoch; epochs must increase from call to call (wrap-around safe).
+ * Later work on the stream sees every store the other ranks made before their
+ * barrier.  A wait longer than timeout_ns stops and sets bit 1 of the peer
+ * status word (never a hang).  No reference counterpart. */
+int cuda_operator_lab_peer_barrier(void* const* flag_arrays, int rank, int world, uint32_t epoch, uint64_t timeout_ns, void* stream);
+
+/* Synchronises the current device, copies the peer status word to *status
+ * (0 = no barrier wait timed out) and with clear != 0 resets it. */
+int cuda_operator_lab_peer_status(unsigned int* status, int clear);
+
 /* Partial sum for the multi-GPU reduction: partial[0] = sum(input[0..n)) in
  * fp64, with the same partition and combine order as the fp32 entry points.
  * Each rank reduces its chunk; an NCCL all-reduce of the doubles then forms

@@ -38,6 +38,8 @@ def _cpu_args(name: str):
         return [f32(2, 8), f32(2, 8)]
     if name.startswith("rmsnorm_rstd_bf16"):
         return [bf(2, 8)]
+    if name == "gemm_swiglu_allgather_bf16":
+        return [bf(2, 8), None, bf(8, 8), [1 << 20], 4]
     if name.startswith("gemm_swiglu_rowscale_bf16"):
         return [bf(2, 8), f32(2), bf(8, 8)]
     if name.startswith("gemm_residual_bf16"):
@@ -63,7 +65,8 @@ ALLOCATING_OPS = sorted(
     name for name in b.__all__
     if not name.endswith("_into") and callable(getattr(b, name))
     and name not in ("gemm_status", "device_info", "build_tag", "library_path",
-                     "fold_rmsnorm_weight")
+                     "fold_rmsnorm_weight", "peer_alloc", "peer_open", "peer_close",
+                     "peer_free", "peer_barrier", "peer_status")
 )
 
 
@@ -106,3 +109,9 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(b, "_LIBRARY", None)
     with pytest.raises(RuntimeError, match="not found"):
         b._library()
+
+
+def test_peer_barrier_rank_checks_before_the_library():
+    for addrs, rank in (([], 0), ([1] * 9, 0), ([1, 2], 2), ([1], -1)):
+        with pytest.raises(ValueError):
+            b.peer_barrier(addrs, rank, 1)

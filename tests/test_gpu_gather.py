@@ -1,0 +1,174 @@
+"""GEMM+SwiGLU with the column all-gather fused into its epilogue (GPU).
+
+On one GPU every rank of a g-way N split is run in turn, each storing its
+column block into g [M, N] buffers of the same device (the epilogue cannot
+tell a peer mapping from a local address): every buffer must equal the
+unsharded GEMM bit for bit.  The device flag barrier is checked for one rank
+and for a wait that runs out (a flag that nothing sets: the kernel must give
+up after its limit, report it in the peer status word and leave the context
+usable).  With two or more GPUs, ranks in separate processes exchange CUDA
+IPC handles and gather over NVLink through ``sharding.PeerColumnGather``.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import seeded
+from cuda_operator_lab import bindings as b
+from cuda_operator_lab import sharding
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _operands(m, k, n, seed):
+    g = seeded(seed)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(DEV)
+    packed = (torch.randn(2 * n, k, generator=g) * k ** -0.5).to(torch.bfloat16).to(DEV)
+    rs = (torch.rand(m, generator=g) + 0.5).to(DEV)
+    return x, packed, rs
+
+
+@pytest.mark.parametrize("scaled", [False, True])
+@pytest.mark.parametrize(("world", "m", "k", "n"), [
+    (2, 512, 1024, 1792), (4, 300, 512, 1024), (8, 256, 2048, 14336 // 8), (8, 130, 256, 1000),
+    (3, 1, 64, 96), (2, 2048, 512, 2 * 112), (2, 640, 512, 2 * 96), (2, 384, 256, 2 * 64)])
+def test_gather_epilogue_fills_every_destination(world, m, k, n, scaled):
+    x, packed, rs = _operands(m, k, n, world * 7 + m)
+    rs = rs if scaled else None
+    if scaled:
+        full = b.gemm_swiglu_rowscale_bf16(x, rs, packed)
+    else:
+        full = b.gemm_swiglu_bf16(x, packed)
+    bufs = [torch.full((m, n), float("nan"), device=DEV, dtype=torch.bfloat16)
+            for _ in range(world)]
+    b.gemm_status(clear=True)
+    for r in range(world):
+        lo, _ = sharding.shard_range(n, r, world)
+        shard = sharding.pack_gate_up_shard(packed, r, world)
+        dests = [bufs[(r + j) % world].data_ptr() + lo * 2 for j in range(world)]
+        b.gemm_swiglu_allgather_bf16(x, rs, shard, dests, n)
+    torch.cuda.synchronize()
+    assert b.gemm_status() == 0
+    for buf in bufs:
+        assert torch.equal(buf, full)
+
+
+def test_gather_argument_checks():
+    x, packed, _ = _operands(64, 64, 64, 1)
+    out = torch.empty(64, 64, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        b.gemm_swiglu_allgather_bf16(x, None, packed, [], 64)
+    with pytest.raises(ValueError):
+        b.gemm_swiglu_allgather_bf16(x, None, packed, [out.data_ptr()] * 9, 64)
+    with pytest.raises(ValueError):
+        b.gemm_swiglu_allgather_bf16(x, None, packed, [out.data_ptr()], 32)
+    # k not a multiple of 8: the tensor path cannot take it (library code 10005)
+    x7 = torch.zeros(64, 60, device=DEV, dtype=torch.bfloat16)
+    w7 = torch.zeros(128, 60, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="10005"):
+        b.gemm_swiglu_allgather_bf16(x7, None, w7, [out.data_ptr()], 64)
+
+
+def test_peer_barrier_single_rank_passes():
+    flags = torch.zeros(8, device=DEV, dtype=torch.int32)
+    b.peer_status(clear=True)
+    for epoch in (1, 2, 3):
+        b.peer_barrier([flags.data_ptr()], 0, epoch)
+    assert b.peer_status() == 0
+    assert flags[0].item() == 3
+
+
+def test_peer_barrier_wait_runs_out_and_reports():
+    """Rank 0 of 2 with nobody playing rank 1: the wait gives up after its
+    limit (20 ms), sets bit 1 of the peer status, and the device stays usable."""
+    flags = torch.zeros(2, 8, device=DEV, dtype=torch.int32)
+    b.peer_status(clear=True)
+    b.peer_barrier([flags[0].data_ptr(), flags[1].data_ptr()], 0, 1, timeout_ns=20_000_000)
+    assert b.peer_status() == 1
+    assert flags[0, 0].item() == 1 and flags[1, 0].item() == 1 and flags[0, 1].item() == 0
+    assert b.peer_status() == 0
+    x, packed, _ = _operands(128, 128, 128, 3)
+    assert torch.equal(b.gemm_swiglu_bf16(x, packed), b.gemm_swiglu_bf16(x, packed))
+
+
+def test_peer_alloc_is_zeroed_and_freed():
+    addr, handle = b.peer_alloc(1 << 20)
+    assert len(handle) == 64 and addr % 256 == 0
+    view = sharding.LibraryPeers().view(addr, 512, 1024)
+    assert int(view.view(torch.int16).abs().sum().item()) == 0
+    del view
+    b.peer_free(addr)
+
+
+def test_peer_column_gather_one_rank():
+    x, packed, rs = _operands(256, 512, 768, 11)
+    gather = sharding.PeerColumnGather(256, 768)
+    try:
+        a = gather(x, packed, rs)
+        first = a.data_ptr()
+        assert torch.equal(a, b.gemm_swiglu_rowscale_bf16(x, rs, packed))
+        c = gather(x, packed)
+        assert c.data_ptr() != first
+        assert torch.equal(c, b.gemm_swiglu_bf16(x, packed))
+        assert gather(x, packed, rs).data_ptr() == first
+        assert b.peer_status() == 0 and b.gemm_status() == 0
+        del a, c
+    finally:
+        gather.close()
+
+
+# ---------------------------------------------------------------- several GPUs
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _ranks_worker(rank: int, world: int, port: int, results) -> None:
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    gather = None
+    try:
+        m, k, n = 1000, 1024, 256 * world
+        x, packed, rs = _operands(m, k, n, 99)  # the same operands on every rank
+        full = b.gemm_swiglu_rowscale_bf16(x, rs, packed)
+        shard = sharding.pack_gate_up_shard(packed, rank, world)
+        gather = sharding.PeerColumnGather(m, n)
+        ok = True
+        for call in range(6):
+            scale = rs * (1 + 0.25 * call)
+            out = gather(x, shard, scale)
+            ok = ok and torch.equal(out, b.gemm_swiglu_rowscale_bf16(x, scale, packed))
+        ok = ok and torch.equal(gather(x, shard, rs), full)
+        del out
+        results[rank] = (ok, b.peer_status(), b.gemm_status())
+    finally:
+        if gather is not None:
+            gather.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_peer_column_gather_across_gpus():
+    world = min(torch.cuda.device_count(), 8)
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_ranks_worker, args=(world, _free_port(), results), nprocs=world,
+                       join=True, start_method="spawn")
+    assert dict(results) == {r: (True, 0, 0) for r in range(world)}

@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import os
 import socket
+from multiprocessing import shared_memory
 
 import pytest
 import torch
@@ -92,3 +93,129 @@ def test_two_gloo_ranks_reproduce_unsharded_results():
     mp.start_processes(_worker, args=(world, _free_port(), results), nprocs=world, join=True,
                        start_method="spawn")
     assert dict(results) == {0: (True, True, True), 1: (True, True, True)}
+
+
+class HostPeers:
+    """Host stand-ins for the peer operations of :class:`sharding.PeerColumnGather`.
+
+    "Device memory" is POSIX shared memory that every rank process can map;
+    an address is (segment number << 40) + byte offset.  The GEMM is the CPU
+    oracle writing its block to every destination with row stride ld; the
+    barrier writes this rank's epoch into slot `rank` of every flag array,
+    meets the other ranks at a gloo barrier and records its own flags -- the
+    protocol of the device barrier, with the waiting done by gloo.
+    """
+
+    def __init__(self) -> None:
+        self.segments: dict[int, shared_memory.SharedMemory] = {}
+        self.next = 1
+        self.epochs_seen: list[list[int]] = []
+
+    def _map(self, shm: shared_memory.SharedMemory) -> int:
+        base = self.next << 40
+        self.next += 1
+        self.segments[base] = shm
+        return base
+
+    def _resolve(self, addr: int) -> tuple[shared_memory.SharedMemory, int]:
+        base = (addr >> 40) << 40
+        return self.segments[base], addr - base
+
+    def alloc(self, nbytes: int) -> tuple[int, bytes]:
+        shm = shared_memory.SharedMemory(create=True, size=nbytes)
+        shm.buf[:nbytes] = bytes(nbytes)
+        return self._map(shm), shm.name.encode()
+
+    def open(self, handle: bytes) -> int:
+        return self._map(shared_memory.SharedMemory(name=handle.decode()))
+
+    def close(self, addr: int) -> None:
+        self.segments.pop(addr).close()
+
+    def free(self, addr: int) -> None:
+        shm = self.segments.pop(addr)
+        shm.close()
+        shm.unlink()
+
+    def view(self, addr: int, m: int, n: int) -> torch.Tensor:
+        shm, off = self._resolve(addr)
+        return torch.frombuffer(shm.buf, dtype=torch.bfloat16, count=m * n, offset=off).view(m, n)
+
+    def gemm(self, x, row_scale, packed_shard, dests, ld) -> None:
+        block = oracle.gemm_swiglu_rowscale_bf16(x, row_scale, packed_shard)
+        m, n = block.shape
+        for d in dests:
+            shm, off = self._resolve(d)
+            rows = torch.frombuffer(shm.buf, dtype=torch.bfloat16, count=(m - 1) * ld + n,
+                                    offset=off)
+            rows.as_strided((m, n), (ld, 1)).copy_(block)
+            del rows
+
+    def barrier(self, flag_addrs, rank, epoch) -> None:
+        world = len(flag_addrs)
+        for a in flag_addrs:
+            shm, off = self._resolve(a)
+            flags = torch.frombuffer(shm.buf, dtype=torch.int32, count=world, offset=off)
+            flags[rank] = epoch
+            del flags
+        dist.barrier()
+        shm, off = self._resolve(flag_addrs[rank])
+        own = torch.frombuffer(shm.buf, dtype=torch.int32, count=world, offset=off).tolist()
+        self.epochs_seen.append(own)
+
+    def status(self) -> int:
+        return 0
+
+
+def _gather_worker(rank: int, world: int, port: int, results) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator()
+        g.manual_seed(4321)
+        m, k, n = 24, 32, 20
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+        packed = (torch.randn(2 * n, k, generator=g) * k ** -0.5).to(torch.bfloat16)
+        rs = torch.rand(m, generator=g) + 0.5
+        peers = HostPeers()
+        gather = sharding.PeerColumnGather(m, n, peers=peers)
+        shard = sharding.pack_gate_up_shard(packed, rank, world)
+        ok = []
+        outs = []
+        for call in range(3):
+            out = gather(x, shard, rs * (1 + call))
+            ok.append(torch.equal(out, oracle.gemm_swiglu_rowscale_bf16(x, rs * (1 + call),
+                                                                         packed)))
+            outs.append(out.data_ptr())
+        alternate = outs[0] == outs[2] != outs[1]
+        first = gather.destinations(0)[0] - gather.addrs[0][rank]
+        epochs = peers.epochs_seen == [[1] * world, [2] * world, [3] * world]
+        del out
+        gather.close()
+        results[rank] = (all(ok), alternate, first == rank * (n // world) * 2, epochs,
+                         not peers.segments)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_column_gather_two_gloo_ranks():
+    """Host logic of the fused GEMM + all-gather: handle exchange, the
+    destination addresses (this rank's column block in every rank's buffer),
+    alternating buffers, epochs of the flag barrier and the collective
+    close."""
+    world = 2
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_gather_worker, args=(world, _free_port(), results), nprocs=world,
+                       join=True, start_method="spawn")
+    assert dict(results) == {r: (True, True, True, True, True) for r in range(world)}
+
+
+def test_peer_column_gather_rejects_bad_shapes():
+    peers = HostPeers()
+    gather = sharding.PeerColumnGather(8, 20, peers=peers)
+    with pytest.raises(ValueError):
+        gather(torch.zeros(4, 8), torch.zeros(40, 8))
+    gather.close()
+    assert not peers.segments
