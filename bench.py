@@ -617,36 +617,41 @@ def gather_variant(d: Dist, x, rstd, folded, out, args) -> dict:
     from cuda_operator_lab import sharding
 
     n_local = N // d.world
-    pg = sharding.PeerColumnGather(M, N)
-    try:
-        def fused():
-            b.rmsnorm_rstd_bf16_into(x, rstd, EPS)
-            pg(x, folded, rstd)
+    fused_ms = {}
+    gathered = {}
+    for layout in ("blocks", "columns"):
+        pg = sharding.PeerColumnGather(M, N, layout=layout)
+        try:
+            def fused():
+                b.rmsnorm_rstd_bf16_into(x, rstd, EPS)
+                pg(x, folded, rstd)
 
-        fused_ms = time_region(d, fused, args.steps, args.warmup)
-        if b.peer_status(clear=True) != 0 or b.gemm_status(clear=True) != 0:
-            raise RuntimeError("peer barrier or GEMM bounded wait timed out in the gather step")
-        gathered = pg.outputs[(pg.calls - 1) % 2]
-        parts = torch.empty(d.world, M, n_local, device=x.device, dtype=torch.bfloat16)
+            fused_ms[layout] = time_region(d, fused, args.steps, args.warmup)
+            if b.peer_status(clear=True) != 0 or b.gemm_status(clear=True) != 0:
+                raise RuntimeError("peer barrier or GEMM bounded wait timed out (gather step)")
+            gathered[layout] = pg.outputs[(pg.calls - 1) % 2].clone()
+        finally:
+            pg.close()
+    parts = torch.empty(d.world, M, n_local, device=x.device, dtype=torch.bfloat16)
 
-        def unfused():
-            b.rmsnorm_rstd_bf16_into(x, rstd, EPS)
-            b.gemm_swiglu_rowscale_bf16_into(x, rstd, folded, out)
-            d.dist.all_gather_into_tensor(parts, out)
+    def unfused():
+        b.rmsnorm_rstd_bf16_into(x, rstd, EPS)
+        b.gemm_swiglu_rowscale_bf16_into(x, rstd, folded, out)
+        d.dist.all_gather_into_tensor(parts, out)
 
-        unfused_ms = time_region(d, unfused, args.steps, args.warmup)
-        same = all(torch.equal(gathered[:, r * n_local:(r + 1) * n_local], parts[r])
-                   for r in range(d.world))
-        same = d.max(0.0 if same else 1.0) == 0.0
-        del gathered, parts
-    finally:
-        pg.close()
+    unfused_ms = time_region(d, unfused, args.steps, args.warmup)
+    same = torch.equal(gathered["blocks"], parts) and all(
+        torch.equal(gathered["columns"][:, r * n_local:(r + 1) * n_local], parts[r])
+        for r in range(d.world))
+    same = d.max(0.0 if same else 1.0) == 0.0
+    del gathered, parts
     link_bytes = (d.world - 1) * M * n_local * 2  # sent by each rank
     link_us = link_bytes / 770e3  # measured peer copy, GB/s per direction
     gemm_us = GEMM_FLOPS / d.world / (peaks()["bf16_tflops_sustained"] * 1e6)
     return {
-        "fused_ms_per_step": round(fused_ms / args.steps, 4),
-        "fused_value": round(GEMM_FLOPS * args.steps / (fused_ms / 1e3) / 1e12, 2),
+        "fused_ms_per_step": round(fused_ms["blocks"] / args.steps, 4),
+        "fused_value": round(GEMM_FLOPS * args.steps / (fused_ms["blocks"] / 1e3) / 1e12, 2),
+        "fused_columns_layout_ms_per_step": round(fused_ms["columns"] / args.steps, 4),
         "nccl_ms_per_step": round(unfused_ms / args.steps, 4),
         "nccl_value": round(GEMM_FLOPS * args.steps / (unfused_ms / 1e3) / 1e12, 2),
         "unit": "TFLOP/s",
@@ -654,7 +659,8 @@ def gather_variant(d: Dist, x, rstd, folded, out, args) -> dict:
         "nvlink_bytes_per_rank": link_bytes,
         "bound_us": round(max(link_us, gemm_us), 1),
         "bound": "nvlink" if link_us > gemm_us else "tensor",
-        "step": "rmsnorm_rstd + GEMM with gathering epilogue + peer flag barrier, vs "
+        "step": "rmsnorm_rstd + GEMM with gathering epilogue + peer flag barrier into "
+                "[g, M, N/g] (the all_gather_into_tensor layout; [M, N] reported beside), vs "
                 "rmsnorm_rstd + GEMM + NCCL all_gather_into_tensor",
     }
 

@@ -158,13 +158,23 @@ class LibraryPeers:
 class PeerColumnGather:
     """N-sharded GEMM+SwiGLU with its column all-gather fused into the GEMM.
 
-    Every rank holds two [M, N] bf16 output buffers in memory the other ranks
-    have mapped (CUDA IPC), plus a flag array.  A call runs the rank's GEMM
-    with the gathering epilogue -- each finished tile of its [M, N/g] column
-    block is stored into the same place of every rank's current buffer, the
-    NVLink transfers overlapping the remaining tiles -- and then the device
-    barrier, after which the returned buffer holds all g blocks.  Everything
-    is stream-ordered on the current stream; the host never waits.
+    Every rank holds two bf16 output buffers of M * N elements in memory the
+    other ranks have mapped (CUDA IPC), plus a flag array.  A call runs the
+    rank's GEMM with the gathering epilogue -- each finished tile of its
+    [M, N/g] column block is stored into the same place of every rank's
+    current buffer, the NVLink transfers overlapping the remaining tiles --
+    and then the device barrier, after which the returned buffer holds all g
+    blocks.  Everything is stream-ordered on the current stream; the host
+    never waits.
+
+    ``layout`` places the blocks: ``"blocks"`` (default) returns
+    [g, M, N/g] with rank r's block contiguous at [r] -- the layout of
+    ``torch.distributed.all_gather_into_tensor``; ``"columns"`` returns the
+    [M, N] matrix itself.  The block layout is the fast one: a tile's rows
+    then lie within one 2 MiB page of each peer's buffer, while in [M, N] a
+    page holds only 2 MiB / (2N) rows and the peer stores of all tiles in
+    flight touch g - 1 times as many pages (measured at 8 GPUs, M = 16384,
+    N = 14336: 0.73 ms per step against 2.6 ms).
 
     The two buffers alternate.  A returned output stays valid until the call
     after the next one, provided each rank reads it on the current stream
@@ -177,7 +187,10 @@ class PeerColumnGather:
     memory, GEMM and barrier operations (default: the CUDA library).
     """
 
-    def __init__(self, m: int, n: int, group=None, peers=None) -> None:
+    def __init__(self, m: int, n: int, group=None, peers=None, layout: str = "blocks") -> None:
+        if layout not in ("blocks", "columns"):
+            raise ValueError("layout must be 'blocks' or 'columns'")
+        self.layout = layout
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         if not 1 <= self.world <= 8:
@@ -209,29 +222,40 @@ class PeerColumnGather:
                     self.addrs[i][j] = self.peers.open(every[j][i])
                     self._opened.append(self.addrs[i][j])
         self.outputs = [self.peers.view(self._local[i], m, n) for i in range(2)]
+        if layout == "blocks":
+            self.outputs = [o.view(self.world, m, self.n_local) for o in self.outputs]
         self.flag_addrs = [self.addrs[0][j] + self._flag_offset for j in range(self.world)]
         self.calls = 0
         if self.world > 1:
             dist.barrier(group=group)  # every mapping exists before any peer store
 
+    @property
+    def ld(self) -> int:
+        """Row stride (elements) of a block in the output buffers."""
+        return self.n_local if self.layout == "blocks" else self.n
+
     def destinations(self, call: int) -> list[int]:
         """Addresses the gathering epilogue of `call` stores to: this rank's
         block in its own buffer first, then in rank+1, rank+2, ... (mod g)."""
         i = call % 2
-        offset = self.rank * self.n_local * 2
+        if self.layout == "blocks":
+            offset = self.rank * self.m * self.n_local * 2
+        else:
+            offset = self.rank * self.n_local * 2
         order = [(self.rank + j) % self.world for j in range(self.world)]
         return [self.addrs[i][r] + offset for r in order]
 
     def __call__(self, x: torch.Tensor, packed_shard: torch.Tensor,
                  row_scale: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's GEMM (packed_shard [2N/g, K], optional row scale) and the
-        gather; returns the [M, N] output holding every rank's block."""
+        gather; returns the output holding every rank's block ([g, M, N/g] or
+        [M, N], see ``layout``)."""
         if x.shape[0] != self.m or packed_shard.shape[0] != 2 * self.n_local:
             raise ValueError(f"expected x[{self.m}, K] and a packed shard of "
                              f"{2 * self.n_local} rows")
         call = self.calls
         self.calls += 1
-        self.peers.gemm(x, row_scale, packed_shard, self.destinations(call), self.n)
+        self.peers.gemm(x, row_scale, packed_shard, self.destinations(call), self.ld)
         self.peers.barrier(self.flag_addrs, self.rank, self.calls)
         return self.outputs[call % 2]
 

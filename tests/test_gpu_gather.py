@@ -108,16 +108,24 @@ def test_peer_alloc_is_zeroed_and_freed():
     b.peer_free(addr)
 
 
-def test_peer_column_gather_one_rank():
+def _as_layout(full: torch.Tensor, world: int, layout: str) -> torch.Tensor:
+    if layout == "columns":
+        return full
+    nl = full.shape[1] // world
+    return torch.stack([full[:, r * nl:(r + 1) * nl] for r in range(world)])
+
+
+@pytest.mark.parametrize("layout", ["blocks", "columns"])
+def test_peer_column_gather_one_rank(layout):
     x, packed, rs = _operands(256, 512, 768, 11)
-    gather = sharding.PeerColumnGather(256, 768)
+    gather = sharding.PeerColumnGather(256, 768, layout=layout)
     try:
         a = gather(x, packed, rs)
         first = a.data_ptr()
-        assert torch.equal(a, b.gemm_swiglu_rowscale_bf16(x, rs, packed))
+        assert torch.equal(a, _as_layout(b.gemm_swiglu_rowscale_bf16(x, rs, packed), 1, layout))
         c = gather(x, packed)
         assert c.data_ptr() != first
-        assert torch.equal(c, b.gemm_swiglu_bf16(x, packed))
+        assert torch.equal(c, _as_layout(b.gemm_swiglu_bf16(x, packed), 1, layout))
         assert gather(x, packed, rs).data_ptr() == first
         assert b.peer_status() == 0 and b.gemm_status() == 0
         del a, c
@@ -134,7 +142,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _ranks_worker(rank: int, world: int, port: int, results) -> None:
+def _ranks_worker(rank: int, world: int, port: int, results, layout: str) -> None:
     from datetime import timedelta
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -149,13 +157,14 @@ def _ranks_worker(rank: int, world: int, port: int, results) -> None:
         x, packed, rs = _operands(m, k, n, 99)  # the same operands on every rank
         full = b.gemm_swiglu_rowscale_bf16(x, rs, packed)
         shard = sharding.pack_gate_up_shard(packed, rank, world)
-        gather = sharding.PeerColumnGather(m, n)
+        gather = sharding.PeerColumnGather(m, n, layout=layout)
         ok = True
         for call in range(6):
             scale = rs * (1 + 0.25 * call)
             out = gather(x, shard, scale)
-            ok = ok and torch.equal(out, b.gemm_swiglu_rowscale_bf16(x, scale, packed))
-        ok = ok and torch.equal(gather(x, shard, rs), full)
+            expected = _as_layout(b.gemm_swiglu_rowscale_bf16(x, scale, packed), world, layout)
+            ok = ok and torch.equal(out, expected)
+        ok = ok and torch.equal(gather(x, shard, rs), _as_layout(full, world, layout))
         del out
         results[rank] = (ok, b.peer_status(), b.gemm_status())
     finally:
@@ -165,10 +174,11 @@ def _ranks_worker(rank: int, world: int, port: int, results) -> None:
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
-def test_peer_column_gather_across_gpus():
+@pytest.mark.parametrize("layout", ["blocks", "columns"])
+def test_peer_column_gather_across_gpus(layout):
     world = min(torch.cuda.device_count(), 8)
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()
-    mp.start_processes(_ranks_worker, args=(world, _free_port(), results), nprocs=world,
-                       join=True, start_method="spawn")
+    mp.start_processes(_ranks_worker, args=(world, _free_port(), results, layout),
+                       nprocs=world, join=True, start_method="spawn")
     assert dict(results) == {r: (True, 0, 0) for r in range(world)}

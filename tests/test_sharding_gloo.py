@@ -167,7 +167,7 @@ class HostPeers:
         return 0
 
 
-def _gather_worker(rank: int, world: int, port: int, results) -> None:
+def _gather_worker(rank: int, world: int, port: int, results, layout: str) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -179,36 +179,40 @@ def _gather_worker(rank: int, world: int, port: int, results) -> None:
         packed = (torch.randn(2 * n, k, generator=g) * k ** -0.5).to(torch.bfloat16)
         rs = torch.rand(m, generator=g) + 0.5
         peers = HostPeers()
-        gather = sharding.PeerColumnGather(m, n, peers=peers)
+        gather = sharding.PeerColumnGather(m, n, peers=peers, layout=layout)
         shard = sharding.pack_gate_up_shard(packed, rank, world)
+        nl = n // world
         ok = []
         outs = []
         for call in range(3):
             out = gather(x, shard, rs * (1 + call))
-            ok.append(torch.equal(out, oracle.gemm_swiglu_rowscale_bf16(x, rs * (1 + call),
-                                                                         packed)))
+            full = oracle.gemm_swiglu_rowscale_bf16(x, rs * (1 + call), packed)
+            if layout == "blocks":
+                full = torch.stack([full[:, r * nl:(r + 1) * nl] for r in range(world)])
+            ok.append(torch.equal(out, full))
             outs.append(out.data_ptr())
         alternate = outs[0] == outs[2] != outs[1]
         first = gather.destinations(0)[0] - gather.addrs[0][rank]
+        first_ok = first == (rank * m * nl * 2 if layout == "blocks" else rank * nl * 2)
         epochs = peers.epochs_seen == [[1] * world, [2] * world, [3] * world]
         del out
         gather.close()
-        results[rank] = (all(ok), alternate, first == rank * (n // world) * 2, epochs,
-                         not peers.segments)
+        results[rank] = (all(ok), alternate, first_ok, epochs, not peers.segments)
     finally:
         dist.destroy_process_group()
 
 
-def test_peer_column_gather_two_gloo_ranks():
+@pytest.mark.parametrize("layout", ["blocks", "columns"])
+def test_peer_column_gather_two_gloo_ranks(layout):
     """Host logic of the fused GEMM + all-gather: handle exchange, the
-    destination addresses (this rank's column block in every rank's buffer),
-    alternating buffers, epochs of the flag barrier and the collective
-    close."""
+    destination addresses (this rank's column block in every rank's buffer,
+    in either layout), alternating buffers, epochs of the flag barrier and
+    the collective close."""
     world = 2
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()
-    mp.start_processes(_gather_worker, args=(world, _free_port(), results), nprocs=world,
-                       join=True, start_method="spawn")
+    mp.start_processes(_gather_worker, args=(world, _free_port(), results, layout),
+                       nprocs=world, join=True, start_method="spawn")
     assert dict(results) == {r: (True, True, True, True, True) for r in range(world)}
 
 
@@ -217,5 +221,7 @@ def test_peer_column_gather_rejects_bad_shapes():
     gather = sharding.PeerColumnGather(8, 20, peers=peers)
     with pytest.raises(ValueError):
         gather(torch.zeros(4, 8), torch.zeros(40, 8))
+    with pytest.raises(ValueError):
+        sharding.PeerColumnGather(8, 20, peers=peers, layout="rows")
     gather.close()
     assert not peers.segments
