@@ -65,6 +65,25 @@ int encode_bf16_rows(CUtensorMap* map, const void* base, std::uint64_t rows, std
   return r == CUDA_SUCCESS ? 0 : col::kErrTensorMapEncode;
 }
 
+// Launch with programmatic stream serialisation (the kernels call
+// griddepcontrol.wait before touching global memory): a GEMM may start its
+// set-up while the previous kernel on the stream finishes.
+template <typename Kernel>
+int launch_serialised(Kernel kernel, int grid, std::uint32_t smem, cudaStream_t s,
+                      const GemmParams& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(col::sm100::kCtaThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, p));
+}
+
 template <int BNH, int EPI, typename TOut, bool FLUSH>
 int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
   using Cfg = TileCfg<BNH, FLUSH ? 1 : 2, col::sm100::epi_smem_reserve(EPI)>;
@@ -79,8 +98,7 @@ int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
   }
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int grid = tiles < sm_count ? tiles : sm_count;
-  kernel<<<grid, col::sm100::kCtaThreads, Cfg::kSmemBytes, s>>>(p);
-  return static_cast<int>(cudaGetLastError());
+  return launch_serialised(kernel, grid, Cfg::kSmemBytes, s, p);
 }
 
 // CTA pairs (2-SM kernel) that can be resident at once on the current device
@@ -121,9 +139,8 @@ int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
   auto kernel = col::sm100::gemm_bf16_tc2_kernel<BNH, EPI, TOut, FLUSH>;
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int grid = 2 * (tiles < clusters ? tiles : clusters);
-  kernel<<<grid, col::sm100::kCtaThreads, Cfg::kSmemBytes, s>>>(p);
   (void)dev;
-  return static_cast<int>(cudaGetLastError());
+  return launch_serialised(kernel, grid, Cfg::kSmemBytes, s, p);
 }
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>

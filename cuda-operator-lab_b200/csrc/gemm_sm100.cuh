@@ -192,6 +192,21 @@ struct TileCfg {
 
 // ------------------------------------------------------------ PTX wrappers
 
+// Programmatic dependent launch.  The GEMM kernels are launched with
+// programmatic stream serialisation: a launch may start while the previous
+// kernel on its stream is still running, so its set-up (barriers, TMEM,
+// tensor-map prefetch) overlaps that kernel's tail.  Every thread that reads
+// or writes global memory first executes grid_dependency_wait(), which returns
+// once the previous grid has completed and its memory is visible (at once
+// when there is none).  grid_dependents_launch() lets the next such launch
+// start its own set-up.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -799,6 +814,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    grid_dependents_launch();
   }
   // Warp 0 (the TMA producer; thread 0 initialised the barriers) needs no
   // TMEM, so it only arrives at the start-up barrier and goes straight to its
@@ -825,6 +841,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
     if (warp == 0) {
       if (lane == 0) {
         // ---------------- TMA producer
+        grid_dependency_wait();
         int stage = 0;
         uint32_t phase = 0;
         uint32_t issued_mask = 0;  // stages holding a copy that may be in flight
@@ -942,6 +959,7 @@ __global__ void __launch_bounds__(kCtaThreads, 1) gemm_bf16_tc_kernel(const __gr
     }
   } else {
     if constexpr (FLUSH && BNH > 96) regs_acquire<kRegsEpilogue>();
+    grid_dependency_wait();
     // ---------------- epilogue: warp w owns TMEM lanes [32q, 32q + 32) with
     // q = w % 4; the kEpiGroups warps of a quarter split its columns.
     const int q = warp & 3;

@@ -161,6 +161,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
     mbar_init(smem_u32(drain_bar), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    grid_dependents_launch();
   }
   if (warp == 2) tmem_alloc_pair(smem_u32(tmem_holder), Cfg::kTmemCols);
   tc_fence_before();
@@ -180,6 +181,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
         // ---------------- TMA producer (both CTAs)
         prefetch_tmap(&p.map_a);
         prefetch_tmap(leader ? &p.map_b0 : &p.map_b1);
+        grid_dependency_wait();
         const CUtensorMap* map_b = leader ? &p.map_b0 : &p.map_b1;
         int stage = 0;
         uint32_t phase = 0;
@@ -303,6 +305,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
     }
   } else {
     if constexpr (FLUSH && BNH > 96) regs_acquire<kRegsEpilogue>();
+    grid_dependency_wait();
     // ---------------- epilogue (both CTAs): this CTA's 128 rows of the tile
     const int q = warp & 3;
     const int group = (warp - 4) >> 2;
