@@ -65,25 +65,6 @@ int encode_bf16_rows(CUtensorMap* map, const void* base, std::uint64_t rows, std
   return r == CUDA_SUCCESS ? 0 : col::kErrTensorMapEncode;
 }
 
-// Launch with programmatic stream serialisation (the kernels call
-// griddepcontrol.wait before touching global memory): a GEMM may start its
-// set-up while the previous kernel on the stream finishes.
-template <typename Kernel>
-int launch_serialised(Kernel kernel, int grid, std::uint32_t smem, cudaStream_t s,
-                      const GemmParams& p) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-  cfg.blockDim = dim3(col::sm100::kCtaThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr.val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, p));
-}
-
 template <int BNH, int EPI, typename TOut, bool FLUSH>
 int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
   using Cfg = TileCfg<BNH, FLUSH ? 1 : 2, col::sm100::epi_smem_reserve(EPI)>;
@@ -98,7 +79,8 @@ int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
   }
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int grid = tiles < sm_count ? tiles : sm_count;
-  return launch_serialised(kernel, grid, Cfg::kSmemBytes, s, p);
+  return col::launch_serialised(kernel, dim3(grid), dim3(col::sm100::kCtaThreads),
+                                 Cfg::kSmemBytes, s, p);
 }
 
 // CTA pairs (2-SM kernel) that can be resident at once on the current device
@@ -140,7 +122,8 @@ int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int grid = 2 * (tiles < clusters ? tiles : clusters);
   (void)dev;
-  return launch_serialised(kernel, grid, Cfg::kSmemBytes, s, p);
+  return col::launch_serialised(kernel, dim3(grid), dim3(col::sm100::kCtaThreads),
+                                 Cfg::kSmemBytes, s, p);
 }
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>
@@ -393,6 +376,7 @@ constexpr std::uint32_t kSplitPairs =
 __global__ void __launch_bounds__(256)
 split_fp32_bf16x3_kernel(const float* __restrict__ src, std::uint64_t rows, std::uint32_t k,
                          std::uint32_t kp, __nv_bfloat16* __restrict__ dst) {
+  col::grid_dependency_wait();
   // One thread per 8 consecutive k of one row: three 16-byte stores.
   const std::uint64_t groups_per_row = kp / 8;
   const std::uint64_t total = rows * groups_per_row;
@@ -426,9 +410,9 @@ int split_fp32(const float* src, std::uint64_t rows, std::uint64_t k, std::uint6
   const std::uint64_t cap = static_cast<std::uint64_t>(col::device_info().sm_count) * 8;
   if (blocks > cap) blocks = cap;
   if (blocks == 0) blocks = 1;
-  split_fp32_bf16x3_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-      src, rows, static_cast<std::uint32_t>(k), static_cast<std::uint32_t>(kp), dst);
-  return static_cast<int>(cudaGetLastError());
+  return col::launch_serialised(split_fp32_bf16x3_kernel, dim3(static_cast<unsigned>(blocks)),
+                                dim3(256), 0, s, src, rows, static_cast<std::uint32_t>(k),
+                                static_cast<std::uint32_t>(kp), dst);
 }
 
 // fp32 GEMM with fused epilogue on tensor cores.  kSwiGLU: w0/w1 are the gate

@@ -49,6 +49,7 @@ __device__ __forceinline__ float load_elem(const T* p, std::size_t i) {
 
 template <typename TIn, int EPI, typename TOut>
 __global__ void __launch_bounds__(kThreads) simt_gemm_kernel(const SimtParams p) {
+  grid_dependency_wait();
   constexpr bool kSwiGLU = (EPI == sm100::kEpiSwiGLU || EPI == sm100::kEpiSwiGLURoundBf16 ||
                            EPI == sm100::kEpiSwiGLURowScale);
   __shared__ float As[kBK][kBM + 4];
@@ -144,8 +145,7 @@ template <typename TIn, int EPI, typename TOut>
 inline int launch_simt(const SimtParams& p, cudaStream_t s) {
   const dim3 grid((p.n + kBN - 1) / kBN, (p.m + kBM - 1) / kBM);
   if (grid.y > 65535u) return static_cast<int>(cudaErrorInvalidValue);
-  simt_gemm_kernel<TIn, EPI, TOut><<<grid, kThreads, 0, s>>>(p);
-  return static_cast<int>(cudaGetLastError());
+  return launch_serialised(simt_gemm_kernel<TIn, EPI, TOut>, grid, dim3(kThreads), 0, s, p);
 }
 
 }  // namespace simt

@@ -192,21 +192,6 @@ struct TileCfg {
 
 // ------------------------------------------------------------ PTX wrappers
 
-// Programmatic dependent launch.  The GEMM kernels are launched with
-// programmatic stream serialisation: a launch may start while the previous
-// kernel on its stream is still running, so its set-up (barriers, TMEM,
-// tensor-map prefetch) overlaps that kernel's tail.  Every thread that reads
-// or writes global memory first executes grid_dependency_wait(), which returns
-// once the previous grid has completed and its memory is visible (at once
-// when there is none).  grid_dependents_launch() lets the next such launch
-// start its own set-up.
-__device__ __forceinline__ void grid_dependency_wait() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-__device__ __forceinline__ void grid_dependents_launch() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

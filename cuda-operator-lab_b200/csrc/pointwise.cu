@@ -46,6 +46,7 @@ unsigned grid_for(std::uint64_t work_items, std::uint64_t wave) {
 __global__ void __launch_bounds__(kThreads)
 swiglu_vec_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
                   float4* __restrict__ o, std::uint64_t nvec) {
+  col::grid_dependency_wait();
   const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
   // Groups of kUnroll strided vectors, the last group predicated, so the
   // ragged end costs one memory round trip like every other group.
@@ -78,6 +79,7 @@ swiglu_vec_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
 __global__ void __launch_bounds__(kThreads)
 swiglu_scalar_kernel(const float* __restrict__ g, const float* __restrict__ u,
                      float* __restrict__ o, std::uint64_t begin, std::uint64_t n) {
+  col::grid_dependency_wait();
   const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
   for (std::uint64_t i = begin + static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
        i < n; i += stride) {
@@ -90,17 +92,20 @@ int swiglu_launch(const float* g, const float* u, float* o, std::uint64_t n, cud
   if (col::aligned16(g) && col::aligned16(u) && col::aligned16(o)) {
     const std::uint64_t nvec = n / 4;
     if (nvec) {
-      swiglu_vec_kernel<<<grid_for(nvec, wave_ctas<swiglu_vec_kernel>()), kThreads, 0, s>>>(
-          reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(u),
+      const int rc = col::launch_serialised(
+          swiglu_vec_kernel, dim3(grid_for(nvec, wave_ctas<swiglu_vec_kernel>())), dim3(kThreads),
+          0, s, reinterpret_cast<const float4*>(g), reinterpret_cast<const float4*>(u),
           reinterpret_cast<float4*>(o), nvec);
+      if (rc != 0) return rc;
       done = nvec * 4;
     }
   }
   if (done < n) {
-    swiglu_scalar_kernel<<<grid_for(n - done, wave_ctas<swiglu_scalar_kernel>()), kThreads, 0, s>>>(
-        g, u, o, done, n);
+    return col::launch_serialised(
+        swiglu_scalar_kernel, dim3(grid_for(n - done, wave_ctas<swiglu_scalar_kernel>())),
+        dim3(kThreads), 0, s, g, u, o, done, n);
   }
-  return static_cast<int>(cudaGetLastError());
+  return 0;
 }
 
 // ---------------------------------------------------------------- bias + GELU
@@ -112,6 +117,7 @@ int swiglu_launch(const float* g, const float* u, float* o, std::uint64_t n, cud
 __global__ void __launch_bounds__(kThreads)
 bias_gelu_vec_kernel(const float4* __restrict__ x, const float4* __restrict__ b,
                      float4* __restrict__ o, std::uint32_t rows, std::uint32_t vcols) {
+  col::grid_dependency_wait();
   const std::uint32_t c = blockIdx.x * kThreads + threadIdx.x;
   if (c >= vcols) return;
   const float4 bv = __ldg(b + c);
@@ -141,6 +147,7 @@ bias_gelu_vec_kernel(const float4* __restrict__ x, const float4* __restrict__ b,
 __global__ void __launch_bounds__(kThreads)
 bias_gelu_scalar_kernel(const float* __restrict__ x, const float* __restrict__ b,
                         float* __restrict__ o, std::uint64_t rows, std::uint32_t cols) {
+  col::grid_dependency_wait();
   const std::uint64_t total = rows * cols;
   const std::uint64_t stride = static_cast<std::uint64_t>(gridDim.x) * kThreads;
   for (std::uint64_t i = static_cast<std::uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
@@ -170,14 +177,14 @@ int bias_gelu(const float* x, const float* b, float* o, std::uint64_t rows, std:
     if (gy > 65535) gy = 65535;
     const std::uint64_t rows_per = (rows + gy - 1) / gy;
     gy = (rows + rows_per - 1) / rows_per;
-    bias_gelu_vec_kernel<<<dim3(gx, static_cast<unsigned>(gy)), kThreads, 0, s>>>(
+    return col::launch_serialised(
+        bias_gelu_vec_kernel, dim3(gx, static_cast<unsigned>(gy)), dim3(kThreads), 0, s,
         reinterpret_cast<const float4*>(x), reinterpret_cast<const float4*>(b),
         reinterpret_cast<float4*>(o), static_cast<std::uint32_t>(rows), vcols);
-  } else {
-    bias_gelu_scalar_kernel<<<grid_for(rows * c, wave_ctas<bias_gelu_scalar_kernel>()), kThreads, 0,
-                              s>>>(x, b, o, rows, c);
   }
-  return static_cast<int>(cudaGetLastError());
+  return col::launch_serialised(
+      bias_gelu_scalar_kernel, dim3(grid_for(rows * c, wave_ctas<bias_gelu_scalar_kernel>())),
+      dim3(kThreads), 0, s, x, b, o, rows, c);
 }
 
 }  // namespace

@@ -135,6 +135,7 @@ sum_kernel(const float* __restrict__ x, std::uint64_t n, std::uint64_t per_cta,
            double* __restrict__ partials, unsigned* __restrict__ counter, void* out) {
   __shared__ double sh[kThreads / 32];
   __shared__ bool is_last;
+  col::grid_dependency_wait();
   const std::uint64_t begin = static_cast<std::uint64_t>(blockIdx.x) * per_cta;
   const std::uint64_t end = min(begin + per_cta, n);
   double acc = 0.0;
@@ -197,11 +198,11 @@ int launch_sum(const float* x, void* out, std::uint64_t n, cudaStream_t s, doubl
                unsigned* counter) {
   const Plan p = plan_for(n);
   if (col::aligned16(x)) {
-    sum_kernel<true, OUT_F64><<<p.ctas, kThreads, 0, s>>>(x, n, p.per_cta, partials, counter, out);
-  } else {
-    sum_kernel<false, OUT_F64><<<p.ctas, kThreads, 0, s>>>(x, n, p.per_cta, partials, counter, out);
+    return col::launch_serialised(sum_kernel<true, OUT_F64>, dim3(p.ctas), dim3(kThreads), 0, s,
+                                  x, n, p.per_cta, partials, counter, out);
   }
-  return static_cast<int>(cudaGetLastError());
+  return col::launch_serialised(sum_kernel<false, OUT_F64>, dim3(p.ctas), dim3(kThreads), 0, s, x,
+                                n, p.per_cta, partials, counter, out);
 }
 
 // Stream-ordered scratch: allocated and freed on the caller's stream, so

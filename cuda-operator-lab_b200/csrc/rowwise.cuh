@@ -153,6 +153,7 @@ template <RowOp OP, typename T, int VEC, int TPR, int NV, bool STORE_H>
 __global__ void __launch_bounds__(TPR * rows_per_cta<TPR>())
 row_kernel(const RowArgs a) {
   constexpr int kRpc = rows_per_cta<TPR>();
+  grid_dependency_wait();
   __shared__ float sh[kRpc * TPR / 32];
 
   const int t = threadIdx.x % TPR;
@@ -387,6 +388,7 @@ __device__ __forceinline__ void st1(T* p, float v) {
 // One CTA per row, rows of any width; the row is re-read once per pass.
 template <RowOp OP, typename T, bool STORE_H>
 __global__ void __launch_bounds__(kLongThreads) row_kernel_long(const RowArgs a) {
+  grid_dependency_wait();
   __shared__ float sh[kLongThreads / 32];
   const std::uint64_t row = blockIdx.x;
   const std::uint32_t cols = a.cols;
@@ -461,9 +463,8 @@ template <RowOp OP, typename T, int VEC, int TPR, int NV, bool STORE_H>
 inline int launch_row_cfg(const RowArgs& a, cudaStream_t s) {
   constexpr int kRpc = rows_per_cta<TPR>();
   const std::uint64_t blocks = (a.rows + kRpc - 1) / kRpc;
-  row_kernel<OP, T, VEC, TPR, NV, STORE_H>
-      <<<static_cast<unsigned>(blocks), TPR * kRpc, 0, s>>>(a);
-  return static_cast<int>(cudaGetLastError());
+  return launch_serialised(row_kernel<OP, T, VEC, TPR, NV, STORE_H>,
+                           dim3(static_cast<unsigned>(blocks)), dim3(TPR * kRpc), 0, s, a);
 }
 
 // units = row width in VEC-element vectors.  Chooses the smallest thread
@@ -479,8 +480,8 @@ inline int dispatch_row_width(std::uint32_t units, const RowArgs& a, cudaStream_
   if (units <= 2048) return launch_row_cfg<OP, T, VEC, 512, 4, STORE_H>(a, s);
   if (units <= 4096) return launch_row_cfg<OP, T, VEC, 1024, 4, STORE_H>(a, s);
   if (units <= 8192) return launch_row_cfg<OP, T, VEC, 1024, 8, STORE_H>(a, s);
-  row_kernel_long<OP, T, STORE_H><<<static_cast<unsigned>(a.rows), kLongThreads, 0, s>>>(a);
-  return static_cast<int>(cudaGetLastError());
+  return launch_serialised(row_kernel_long<OP, T, STORE_H>, dim3(static_cast<unsigned>(a.rows)),
+                           dim3(kLongThreads), 0, s, a);
 }
 
 template <RowOp OP, typename T, bool STORE_H>

@@ -102,14 +102,15 @@ class HostPeers:
     an address is (segment number << 40) + byte offset.  The GEMM is the CPU
     oracle writing its block to every destination with row stride ld; the
     barrier writes this rank's epoch into slot `rank` of every flag array,
-    meets the other ranks at a gloo barrier and records its own flags -- the
-    protocol of the device barrier, with the waiting done by gloo.
+    meets the other ranks at a gloo barrier and checks that every slot of its
+    own array has reached the epoch -- the protocol of the device barrier, with
+    the waiting done by gloo.
     """
 
     def __init__(self) -> None:
         self.segments: dict[int, shared_memory.SharedMemory] = {}
         self.next = 1
-        self.epochs_seen: list[list[int]] = []
+        self.epochs_seen: list[bool] = []
 
     def _map(self, shm: shared_memory.SharedMemory) -> int:
         base = self.next << 40
@@ -161,7 +162,8 @@ class HostPeers:
         dist.barrier()
         shm, off = self._resolve(flag_addrs[rank])
         own = torch.frombuffer(shm.buf, dtype=torch.int32, count=world, offset=off).tolist()
-        self.epochs_seen.append(own)
+        # another rank may already have arrived at the next epoch: at least this one
+        self.epochs_seen.append(all(v >= epoch for v in own))
 
     def status(self) -> int:
         return 0
@@ -194,7 +196,7 @@ def _gather_worker(rank: int, world: int, port: int, results, layout: str) -> No
         alternate = outs[0] == outs[2] != outs[1]
         first = gather.destinations(0)[0] - gather.addrs[0][rank]
         first_ok = first == (rank * m * nl * 2 if layout == "blocks" else rank * nl * 2)
-        epochs = peers.epochs_seen == [[1] * world, [2] * world, [3] * world]
+        epochs = peers.epochs_seen == [True] * 3
         del out
         gather.close()
         results[rank] = (all(ok), alternate, first_ok, epochs, not peers.segments)
