@@ -16,7 +16,9 @@ needed).  Scaling is strong: the total work is fixed and rank r of N owns
 output columns [r*N/g, (r+1)*N/g).
 
 Extra keys: ``e2e`` (the same metric through the public API with the X copy
-from pinned host memory and the output shard copied back inside every step),
+from pinned host memory and the output shard copied back inside every step,
+uploads, compute and downloads of consecutive steps overlapped on three
+streams; ``serial_value`` without the overlap),
 ``roofline`` (the GEMM kernel against the measured sustained bf16 peak),
 ``cpu_baseline`` (the CPU oracle on a row sample, rank 0 at N=1), ``clocks``
 (nvidia-smi sampled during the timed region), ``gpu_launches`` and ``ops``
@@ -215,16 +217,25 @@ def make_inputs(d: Dist, device: torch.device) -> dict:
 # ---------------------------------------------------------------- our arm
 
 
-def time_region(d: Dist, fn, steps: int, warmup: int) -> float:
-    """Max over ranks of the device time (ms) of `steps` calls of fn."""
+def time_region(d: Dist, fn, steps: int, warmup: int, drain=None, after_start=None) -> float:
+    """Max over ranks of the device time (ms) of `steps` calls of fn.  When fn
+    also uses other streams, `after_start(start_event)` makes them wait for the
+    start event and `drain()` makes the current stream wait for their last
+    work, so the timed region covers it."""
     for _ in range(warmup):
         fn()
+    if drain is not None:
+        drain()
     d.barrier()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record()
+    if after_start is not None:
+        after_start(start)
     for _ in range(steps):
         fn()
+    if drain is not None:
+        drain()
     end.record()
     end.synchronize()
     ms = start.elapsed_time(end)
@@ -539,21 +550,61 @@ def run_ours(args, d: Dist) -> dict | None:
     achieved = flops_launch / gemm_us / 1e6
     traffic = committed_traffic().get(f"gemm_swiglu_rowscale_bf16_M{M}_K{K}_N{n_local}")
 
-    # e2e through the public API: pinned host X in, output shard back, every step
+    # e2e through the public API: pinned host X in, output shard back, every step.
+    # Serving-style pipeline: step i's X upload (copy stream), RMSNorm+GEMM (this
+    # stream) and output download (second copy stream) overlap steps i-1 and i+1,
+    # with two device and two pinned host buffers.  The serial form (upload,
+    # compute, download on one stream) is reported beside it.
     x_host = x.cpu().pin_memory()
-    out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-    x_dev = torch.empty_like(x)
+    out_host = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
+    x_dev = [torch.empty_like(x) for _ in range(2)]
+    out_dev = [out, torch.empty_like(out)]
+    rstd_dev = [rstd, torch.empty_like(rstd)]
+    main = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+    downloaded = [torch.cuda.Event() for _ in range(2)]
+    e2e_index = [0]
 
     def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        b.rmsnorm_rstd_bf16_into(x_dev, rstd, EPS)
-        b.gemm_swiglu_rowscale_bf16_into(x_dev, rstd, folded, out)
-        out_host.copy_(out, non_blocking=True)
+        j = e2e_index[0] % 2
+        e2e_index[0] += 1
+        with torch.cuda.stream(up):
+            up.wait_event(computed[j])  # step i-2 has finished reading x_dev[j]
+            x_dev[j].copy_(x_host, non_blocking=True)
+            uploaded[j].record(up)
+        main.wait_event(uploaded[j])
+        main.wait_event(downloaded[j])  # step i-2's output has left out_dev[j]
+        b.rmsnorm_rstd_bf16_into(x_dev[j], rstd_dev[j], EPS)
+        b.gemm_swiglu_rowscale_bf16_into(x_dev[j], rstd_dev[j], folded, out_dev[j])
+        computed[j].record(main)
+        with torch.cuda.stream(down):
+            down.wait_event(computed[j])
+            out_host[j].copy_(out_dev[j], non_blocking=True)
+            downloaded[j].record(down)
 
-    e2e_steps = max(5, args.steps // 20)
-    e2e_ms = time_region(d, e2e_step, e2e_steps, 2)
-    torch.testing.assert_close(out_host[:4].float(), out[:4].cpu().float())
-    del x_host, out_host, x_dev
+    def e2e_drain():
+        for ev in downloaded:
+            main.wait_event(ev)
+
+    def e2e_serial_step():
+        x_dev[0].copy_(x_host, non_blocking=True)
+        b.rmsnorm_rstd_bf16_into(x_dev[0], rstd, EPS)
+        b.gemm_swiglu_rowscale_bf16_into(x_dev[0], rstd, folded, out)
+        out_host[0].copy_(out, non_blocking=True)
+
+    e2e_steps = max(6, args.steps // 20)
+    def e2e_start(ev):
+        up.wait_event(ev)
+        down.wait_event(ev)
+
+    e2e_ms = time_region(d, e2e_step, e2e_steps, 2, drain=e2e_drain, after_start=e2e_start)
+    last = (e2e_index[0] - 1) % 2
+    torch.testing.assert_close(out_host[last][:4].float(), out_dev[last][:4].cpu().float())
+    e2e_serial_ms = time_region(d, e2e_serial_step, e2e_steps, 2)
+    torch.testing.assert_close(out_host[0][:4].float(), out[:4].cpu().float())
+    del x_host, out_host, x_dev, out_dev, rstd_dev
 
     gather = gather_variant(d, x, rstd, folded, out, args) if d.world > 1 and args.gather else None
 
@@ -588,7 +639,9 @@ def run_ours(args, d: Dist) -> dict | None:
                    "l2": "inputs larger than L2 (X 134 MB, W 235 MB); no flush"},
         "e2e": {"value": round(GEMM_FLOPS * e2e_steps / (e2e_ms / 1e3) / 1e12, 2),
                 "unit": "TFLOP/s", "h2d_bytes_per_step": M * K * 2 * d.world,
-                "d2h_bytes_per_step": M * N * 2},
+                "d2h_bytes_per_step": M * N * 2,
+                "pipeline": "upload / RMSNorm+GEMM / download on three streams, two buffers",
+                "serial_value": round(GEMM_FLOPS * e2e_steps / (e2e_serial_ms / 1e3) / 1e12, 2)},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
                      "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": round(achieved / pk["bf16_tflops_sustained"], 3),
