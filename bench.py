@@ -752,8 +752,19 @@ class CpuPath:
         dt = self.run(rows)
         flops = 2 * rows * K * 2 * N
         return {"value": round(flops / dt / 1e12, 4), "unit": "TFLOP/s",
-                "cores": torch.get_num_threads(), "kind": "port",
+                "cores": torch.get_num_threads(), "cpu_model": cpu_model(), "kind": "port",
                 "sample": f"{rows} of {M} rows of X against the full W, one pass ({dt:.2f} s)"}
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def cpu_baseline(seconds: float = 15.0) -> dict:
@@ -787,7 +798,8 @@ def run_reference(args) -> dict:
                    "sample_rows_per_step": rows,
                    "path": "reference CPU math (oracle port of references.py) on host cores"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": samples[0]["cores"],
-                         "kind": "port", "sample": samples[0]["sample"]},
+                         "cpu_model": samples[0]["cpu_model"], "kind": "port",
+                         "sample": samples[0]["sample"]},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
