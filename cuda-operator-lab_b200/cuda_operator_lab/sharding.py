@@ -203,24 +203,37 @@ class PeerColumnGather:
         out_bytes = m * n * 2
         self._flag_offset = -(-out_bytes // 256) * 256
         nbytes = self._flag_offset + _FLAG_BYTES
-        local = [self.peers.alloc(nbytes) for _ in range(2)]
-        self._local = [addr for addr, _ in local]
-        handles = [h for _, h in local]
-        every = [None] * self.world
-        if self.world > 1:
-            dist.all_gather_object(every, handles, group=group)
-        else:
-            every = [handles]
-        # addrs[i][j]: rank j's buffer i as mapped here
+        self._local: list[int] | None = []
         self._opened: list[int] = []
-        self.addrs = [[0] * self.world for _ in range(2)]
-        for j in range(self.world):
-            for i in range(2):
-                if j == self.rank:
-                    self.addrs[i][j] = self._local[i]
-                else:
-                    self.addrs[i][j] = self.peers.open(every[j][i])
-                    self._opened.append(self.addrs[i][j])
+        handles: list[bytes] = []
+        try:
+            for _ in range(2):
+                addr, handle = self.peers.alloc(nbytes)
+                self._local.append(addr)
+                handles.append(handle)
+            every = [None] * self.world
+            if self.world > 1:
+                dist.all_gather_object(every, handles, group=group)
+            else:
+                every = [handles]
+            # addrs[i][j]: rank j's buffer i as mapped here
+            self.addrs = [[0] * self.world for _ in range(2)]
+            for j in range(self.world):
+                for i in range(2):
+                    if j == self.rank:
+                        self.addrs[i][j] = self._local[i]
+                    else:
+                        self.addrs[i][j] = self.peers.open(every[j][i])
+                        self._opened.append(self.addrs[i][j])
+        except Exception:
+            # release what this rank holds; the other ranks' next collective on
+            # `group` then fails with the process group's timeout
+            for addr in self._opened:
+                self.peers.close(addr)
+            for addr in self._local:
+                self.peers.free(addr)
+            self._local = None
+            raise
         self.outputs = [self.peers.view(self._local[i], m, n) for i in range(2)]
         if layout == "blocks":
             self.outputs = [o.view(self.world, m, self.n_local) for o in self.outputs]
@@ -260,7 +273,8 @@ class PeerColumnGather:
         return self.outputs[call % 2]
 
     def close(self) -> None:
-        """Unmaps the peers' buffers and frees this rank's (collective)."""
+        """Unmaps the peers' buffers and frees this rank's (collective).  Output
+        tensors returned by earlier calls must not be used afterwards."""
         if self._local is None:
             return
         if torch.cuda.is_available():

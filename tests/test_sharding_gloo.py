@@ -227,3 +227,21 @@ def test_peer_column_gather_rejects_bad_shapes():
         sharding.PeerColumnGather(8, 20, peers=peers, layout="rows")
     gather.close()
     assert not peers.segments
+
+
+def test_peer_column_gather_releases_memory_when_setup_fails():
+    class FailingPeers(HostPeers):
+        def __init__(self) -> None:
+            super().__init__()
+            self.allocs = 0
+
+        def alloc(self, nbytes):
+            self.allocs += 1
+            if self.allocs == 2:
+                raise RuntimeError("CUDA error 2: out of memory")
+            return super().alloc(nbytes)
+
+    peers = FailingPeers()
+    with pytest.raises(RuntimeError, match="out of memory"):
+        sharding.PeerColumnGather(8, 20, peers=peers)
+    assert not peers.segments  # the first buffer was freed again
