@@ -155,14 +155,15 @@ enum class BMode { kSwiGLU, kGelu };
 // than BNH=96 (65 waves, which a pure MMA-column model would pick); M=512,
 // N=4096 SwiGLU runs BNH=112 (74 tiles, one wave).
 constexpr std::uint64_t kKBlockFloor = 1365;
+constexpr int kNarrowMaxKBlocks = 16;
 
 int choose_bnh(int mblocks, std::uint64_t n, bool swiglu, int sm_count, int max_bnh,
-               bool with112) {
-  constexpr int kCandidates[] = {128, 112, 96, 64};
+               bool with112, bool with32) {
+  constexpr int kCandidates[] = {128, 112, 96, 64, 32};
   int best = 64;
   std::uint64_t best_cost = ~0ull;
   for (int bnh : kCandidates) {
-    if (bnh > max_bnh || (bnh == 112 && !with112)) continue;
+    if (bnh > max_bnh || (bnh == 112 && !with112) || (bnh == 32 && !with32)) continue;
     const std::uint64_t cols = swiglu ? bnh : 2 * bnh;
     const std::uint64_t tiles = static_cast<std::uint64_t>(mblocks) * ((n + cols - 1) / cols);
     const std::uint64_t waves = (tiles + sm_count - 1) / sm_count;
@@ -252,8 +253,11 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
   const int mblocks_sched = use_pair ? (mblocks + 1) / 2 : mblocks;
   int max_bnh = 128;
   if constexpr (FLUSH) max_bnh = flush_wide_ok<EPI, TOut>(use_pair) ? 128 : 96;
+  // BNH = 32 (twice the tiles of 64, each with half the B box and half the
+  // epilogue) only where a tile's fixed cost outweighs its main loop.
+  const bool with32 = !FLUSH && ops.k_blocks <= kNarrowMaxKBlocks;
   const int bnh = choose_bnh(mblocks_sched, n, mode == BMode::kSwiGLU,
-                             use_pair ? pair_slots : info.sm_count, max_bnh, !FLUSH);
+                             use_pair ? pair_slots : info.sm_count, max_bnh, !FLUSH, with32);
 
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
@@ -324,6 +328,9 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
         case 96:
           if ((rc = set_smem_attr_2sm<96, EPI, TOut, false>(dev))) return rc;
           return launch_tc2<96, EPI, TOut, false>(p, s, dev, pair_slots);
+        case 32:
+          if ((rc = set_smem_attr_2sm<32, EPI, TOut, false>(dev))) return rc;
+          return launch_tc2<32, EPI, TOut, false>(p, s, dev, pair_slots);
         default:
           if ((rc = set_smem_attr_2sm<64, EPI, TOut, false>(dev))) return rc;
           return launch_tc2<64, EPI, TOut, false>(p, s, dev, pair_slots);
@@ -333,6 +340,7 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
       case 128: return launch_tc<128, EPI, TOut, false>(p, s, dev, info.sm_count);
       case 112: return launch_tc<112, EPI, TOut, false>(p, s, dev, info.sm_count);
       case 96: return launch_tc<96, EPI, TOut, false>(p, s, dev, info.sm_count);
+      case 32: return launch_tc<32, EPI, TOut, false>(p, s, dev, info.sm_count);
       default: return launch_tc<64, EPI, TOut, false>(p, s, dev, info.sm_count);
     }
   }
