@@ -89,7 +89,8 @@ int launch_tc(GemmParams& p, cudaStream_t s, int dev, int sm_count) {
 // the answer).  Queried once per device; 0 if clusters are unavailable.
 template <int EPI, typename TOut>
 int max_pair_clusters(int dev) {
-  using Cfg = col::sm100::TileCfg2<128, 2, col::sm100::epi_smem_reserve(EPI)>;
+  using Cfg = col::sm100::TileCfg2<128, col::sm100::pair_kps(128, EPI, false),
+                                    col::sm100::epi_smem_reserve(EPI)>;
   static int cached[64] = {};
   static std::once_flag flags[64];
   std::call_once(flags[dev & 63], [dev]() {
@@ -117,7 +118,8 @@ int max_pair_clusters(int dev) {
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>
 int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
-  using Cfg = col::sm100::TileCfg2<BNH, FLUSH ? 1 : 2, col::sm100::epi_smem_reserve(EPI)>;
+  using Cfg = col::sm100::TileCfg2<BNH, col::sm100::pair_kps(BNH, EPI, FLUSH),
+                                    col::sm100::epi_smem_reserve(EPI)>;
   auto kernel = col::sm100::gemm_bf16_tc2_kernel<BNH, EPI, TOut, FLUSH>;
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int grid = 2 * (tiles < clusters ? tiles : clusters);
@@ -128,7 +130,8 @@ int launch_tc2(GemmParams& p, cudaStream_t s, int dev, int clusters) {
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>
 int set_smem_attr_2sm(int dev) {
-  using Cfg = col::sm100::TileCfg2<BNH, FLUSH ? 1 : 2, col::sm100::epi_smem_reserve(EPI)>;
+  using Cfg = col::sm100::TileCfg2<BNH, col::sm100::pair_kps(BNH, EPI, FLUSH),
+                                    col::sm100::epi_smem_reserve(EPI)>;
   static std::atomic<std::uint64_t> attr_set{0};
   const std::uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set.load(std::memory_order_acquire) & bit)) {

@@ -27,9 +27,21 @@ namespace sm100 {
 
 // KPS = k-blocks per pipeline stage, as in TileCfg.
 template <int BNH, int KPS = 1, uint32_t RESERVE = 0>
+struct TileCfg2;
+
+// k-blocks per stage of the pair kernel: the most operand bytes in flight.
+// Mid-size GEMMs wait on L2 round trips, so throughput per SM follows the
+// bytes the ring holds: at BNH = 64 three-k-block stages hold 216 KB (three
+// stages) where two-k-block stages hold 192 KB (four); elsewhere two.  FLUSH
+// kernels keep one (their accumulation chunks end on k-block boundaries).
+constexpr int pair_kps(int bnh, int epi, bool flush) {
+  return flush ? 1 : (bnh == 64 && epi_smem_reserve(epi) == 0 ? 3 : 2);
+}
+
+template <int BNH, int KPS, uint32_t RESERVE>
 struct TileCfg2 {
   static_assert(BNH % 16 == 0 && BNH >= 32 && BNH <= 128, "unsupported B box height");
-  static_assert(KPS == 1 || KPS == 2, "one or two k-blocks per stage");
+  static_assert(KPS >= 1 && KPS <= 3, "one to three k-blocks per stage");
   static constexpr int kMmaM = 256;
   static constexpr int kMmaN = 2 * BNH;
   static constexpr uint32_t kABytes = kBlockM * kBlockK * 2;  // this CTA's 128 rows
@@ -123,7 +135,7 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols)
 template <int BNH, int EPI, typename TOut, bool FLUSH = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ GemmParams p) {
-  constexpr int kKps = FLUSH ? 1 : 2;
+  constexpr int kKps = pair_kps(BNH, EPI, FLUSH);
   using Cfg = TileCfg2<BNH, kKps, epi_smem_reserve(EPI)>;
   static_assert(EPI != kEpiSwiGLUGather || (sizeof(TOut) == 2 && !FLUSH), "gather: bf16 out");
   constexpr int kStages = Cfg::kStages;
