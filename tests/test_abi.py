@@ -73,3 +73,38 @@ def test_error_strings_cover_library_codes():
         assert str(exc).startswith("CUDA error 1:")
     else:
         raise AssertionError("check(1) did not raise")
+
+
+def test_plain_c_program_links_against_the_library(tmp_path):
+    """A C99 caller (no PyTorch, no CUDA headers beyond the library's) includes
+    the header, links the shared library and calls its host-only entry points."""
+    import shutil
+
+    import pytest
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    libdir = library().parent
+    src = tmp_path / "caller.c"
+    src.write_text(
+        '#include "cuda_operator_lab.h"\n'
+        "#include <stdio.h>\n"
+        "#include <string.h>\n"
+        "int main(void) {\n"
+        "  const char* tag = cuda_operator_lab_build_tag();\n"
+        "  const char* msg = cuda_operator_error_string(10005);\n"
+        "  if (!tag || !strstr(tag, \"sm_100a\") || !msg || !strstr(msg, \"gathering\")) return 1;\n"
+        "  if (cuda_operator_lab_peer_handle_bytes() != 64) return 2;\n"
+        "  printf(\"%s\\n\", tag);\n"
+        "  return 0;\n"
+        "}\n")
+    exe = tmp_path / "caller"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", f"-I{ROOT / 'include'}", str(src),
+                    f"-L{libdir}", "-lcuda_operator_lab", f"-Wl,-rpath,{libdir}", "-o", str(exe)],
+                   check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, out
+    assert "sm_100a" in out.stdout
+    # the header is also valid C++
+    subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-x", "c++", f"-I{ROOT / 'include'}",
+                    str(HEADER)], check=True)
