@@ -68,6 +68,7 @@ struct DeviceInfo {
   int cc_major = 0;
   int cc_minor = 0;
   int max_smem_optin = 0;
+  int l2_bytes = 0;
 };
 
 // Library-owned stream-ordered memory pool of the current device (freed
@@ -93,6 +94,7 @@ inline const DeviceInfo& device_info(int* device_out = nullptr) {
     cudaDeviceGetAttribute(&info.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&info.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
     cudaDeviceGetAttribute(&info.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&info.l2_bytes, cudaDevAttrL2CacheSize, dev);
     if (info.sm_count <= 0) info.sm_count = 148;
     infos[dev] = info;
   });
@@ -171,6 +173,7 @@ __device__ __forceinline__ float bf16_round(float x) {
 // Streaming (evict-first) 16-byte load for read-once inputs whose data is not
 // needed again (the global reduction).
 __device__ __forceinline__ float4 ld_stream_f4(const float4* p) { return __ldcs(p); }
+__device__ __forceinline__ float4 ld_cached_f4(const float4* p) { return __ldg(p); }
 
 __device__ __forceinline__ void unpack_bf16x8(uint4 v, float (&f)[8]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
