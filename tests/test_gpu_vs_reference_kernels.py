@@ -55,14 +55,20 @@ def _s() -> ctypes.c_void_p:
 
 
 def _time_us(fn, reps=20) -> float:
-    """fn() takes no arguments and enqueues on torch's current stream."""
-    for _ in range(3):
-        fn()
+    """fn() takes no arguments and enqueues on torch's current stream.  The
+    warm-up calls run on the stream that is then captured, as a caller that
+    graphs its steady state would (the library keeps per-stream scratch for
+    the reduction; a stream it has not served yet gets graph memory nodes)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     try:
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        with torch.cuda.graph(graph, stream=side):
             for _ in range(reps):
                 fn()
         graph.replay()
