@@ -244,9 +244,9 @@ int reduce_with_pool_scratch(const float* x, void* out, std::uint64_t n, cudaStr
 // ordered, and different streams get different blocks, so the counter is
 // zero whenever a launch starts and a call is a single kernel launch.  The
 // block is created on the first call on a stream (cudaMalloc plus a memset
-// on that stream); a stream that is being captured into a graph, more than
-// kMaxStreamScratch streams, and cudaStreamPerThread (one handle naming a
-// different stream on every host thread) use the stream-ordered pool path.
+// on that stream); calls captured into a graph, more than kMaxStreamScratch
+// streams, and cudaStreamPerThread (one handle naming a different stream on
+// every host thread) use the stream-ordered pool path.
 constexpr int kMaxStreamScratch = 256;
 
 struct StreamScratch {
@@ -265,6 +265,15 @@ bool stream_scratch(cudaStream_t s, unsigned ctas, double** partials, unsigned**
   const unsigned capacity = static_cast<unsigned>(col::device_info().sm_count) *
                             static_cast<unsigned>(resident_ctas_per_sm());
   if (ctas > capacity || s == cudaStreamPerThread) return false;
+  // A captured call never uses the stream's block: the graph may later run on
+  // another stream, concurrently with calls on this one, and the two would
+  // share partials and counter.  It takes graph-owned scratch instead.
+  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &capturing) != cudaSuccess ||
+      capturing != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return false;
+  }
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < used; ++i) {
     if (entries[i].device == dev && entries[i].stream == s) {
@@ -274,12 +283,6 @@ bool stream_scratch(cudaStream_t s, unsigned ctas, double** partials, unsigned**
     }
   }
   if (used == kMaxStreamScratch) return false;
-  cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(s, &capturing) != cudaSuccess ||
-      capturing != cudaStreamCaptureStatusNone) {
-    cudaGetLastError();
-    return false;
-  }
   void* block = nullptr;
   const std::size_t bytes = static_cast<std::size_t>(capacity) * sizeof(double) + 256;
   if (cudaMalloc(&block, bytes) != cudaSuccess) {
