@@ -256,6 +256,58 @@ struct StreamScratch {
   unsigned* counter;
 };
 
+// Blocks for captured calls.  A captured call must not embed a stream's
+// block (the graph may run on another stream, concurrently with that stream's
+// own calls), so it takes a block of its own for good: kCaptureBlocks of them
+// per device are made, counters zeroed and synchronised, by the first
+// non-captured call on the device; once they are used up, captured calls take
+// stream-ordered scratch (graph memory nodes and a counter memset).
+constexpr int kCaptureBlocks = 64;
+
+struct CaptureBlocks {
+  double* base = nullptr;
+  int next = 0;
+  bool tried = false;
+};
+
+std::mutex capture_mu;
+CaptureBlocks capture_blocks[64];
+
+std::size_t block_stride(unsigned capacity) {
+  return (static_cast<std::size_t>(capacity) * sizeof(double) + 256 + 255) / 256 * 256;
+}
+
+// Called outside any capture, with capture_mu held.
+void make_capture_blocks(int dev, unsigned capacity, cudaStream_t s) {
+  CaptureBlocks& cb = capture_blocks[dev & 63];
+  if (cb.tried) return;
+  cb.tried = true;
+  const std::size_t stride = block_stride(capacity);
+  void* base = nullptr;
+  if (cudaMalloc(&base, stride * kCaptureBlocks) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  if (cudaMemsetAsync(base, 0, stride * kCaptureBlocks, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(base);
+    return;
+  }
+  cb.base = static_cast<double*>(base);
+}
+
+bool capture_scratch(int dev, unsigned capacity, double** partials, unsigned** counter) {
+  std::lock_guard<std::mutex> lock(capture_mu);
+  CaptureBlocks& cb = capture_blocks[dev & 63];
+  if (cb.base == nullptr || cb.next == kCaptureBlocks) return false;
+  double* p = reinterpret_cast<double*>(reinterpret_cast<char*>(cb.base) +
+                                        block_stride(capacity) * static_cast<std::size_t>(cb.next++));
+  *partials = p;
+  *counter = reinterpret_cast<unsigned*>(p + capacity);
+  return true;
+}
+
 bool stream_scratch(cudaStream_t s, unsigned ctas, double** partials, unsigned** counter) {
   static std::mutex mu;
   static StreamScratch entries[kMaxStreamScratch];
@@ -267,12 +319,18 @@ bool stream_scratch(cudaStream_t s, unsigned ctas, double** partials, unsigned**
   if (ctas > capacity || s == cudaStreamPerThread) return false;
   // A captured call never uses the stream's block: the graph may later run on
   // another stream, concurrently with calls on this one, and the two would
-  // share partials and counter.  It takes graph-owned scratch instead.
+  // share partials and counter.
   cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(s, &capturing) != cudaSuccess ||
-      capturing != cudaStreamCaptureStatusNone) {
+  if (cudaStreamIsCapturing(s, &capturing) != cudaSuccess) {
     cudaGetLastError();
     return false;
+  }
+  if (capturing != cudaStreamCaptureStatusNone) {
+    return capture_scratch(dev, capacity, partials, counter);
+  }
+  {
+    std::lock_guard<std::mutex> lock(capture_mu);
+    make_capture_blocks(dev, capacity, s);
   }
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < used; ++i) {
