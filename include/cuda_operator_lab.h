@@ -44,11 +44,14 @@ extern "C" {
  * fp32 atomicAdd combine, reduction.cu:43, is not).  input may be NULL only
  * when n == 0, in which case out[0] = 0.  Scratch (8 bytes per CTA, one
  * resident wave of CTAs) is a block the library allocates once per
- * (device, stream) on the first call on that stream and keeps; while a
- * stream is being captured, and for cudaStreamPerThread, it is a
- * stream-ordered allocation from a library-owned cudaMemPool instead.  A
- * stream handle must not be destroyed and re-created (same value) while
- * the old stream still has a reduction in flight. */
+ * (device, stream) on the first call on that stream and keeps (the first
+ * call on a device also reserves 64 blocks for captured calls and waits for
+ * its stream once).  A call captured into a CUDA graph takes one of those
+ * reserved blocks for good, never the stream's; beyond them, and for
+ * cudaStreamPerThread, the scratch is a stream-ordered allocation from a
+ * library-owned cudaMemPool (graph memory nodes under capture).  A stream
+ * handle must not be destroyed and re-created (same value) while the old
+ * stream still has a reduction in flight. */
 int cuda_operator_reduction_v0(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:8  */
 int cuda_operator_reduction_v1(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:14 */
 int cuda_operator_reduction_v2(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:20 */
