@@ -245,3 +245,45 @@ def test_peer_column_gather_releases_memory_when_setup_fails():
     with pytest.raises(RuntimeError, match="out of memory"):
         sharding.PeerColumnGather(8, 20, peers=peers)
     assert not peers.segments  # the first buffer was freed again
+
+
+@pytest.mark.parametrize("layout", ["blocks", "columns"])
+def test_peer_column_gather_destinations_at_eight_ranks(monkeypatch, layout):
+    """Destination arithmetic of rank 3 of 8 (one process; the collective calls
+    replaced): its block goes to its own buffer first, then to ranks 4, 5, ...,
+    2, at the block's origin in each rank's buffer of the current call."""
+    world, rank, m, n = 8, 3, 6, 64
+    peers = HostPeers()
+    handles_seen = []
+    others = []  # the other ranks' buffers, made here
+
+    def all_gather_object(out, obj, group=None):
+        handles_seen.append(obj)
+        for j in range(world):
+            if j == rank:
+                out[j] = obj
+                continue
+            made = [peers.alloc(4096) for _ in range(2)]
+            others.extend(addr for addr, _ in made)
+            out[j] = [handle for _, handle in made]
+
+    monkeypatch.setattr(sharding.dist, "is_initialized", lambda: True)
+    monkeypatch.setattr(sharding.dist, "get_world_size", lambda group=None: world)
+    monkeypatch.setattr(sharding.dist, "get_rank", lambda group=None: rank)
+    monkeypatch.setattr(sharding.dist, "all_gather_object", all_gather_object)
+    monkeypatch.setattr(sharding.dist, "barrier", lambda group=None: None)
+    gather = sharding.PeerColumnGather(m, n, peers=peers, layout=layout)
+    nl = n // world
+    for call in range(3):
+        dests = gather.destinations(call)
+        order = [(rank + j) % world for j in range(world)]
+        offset = rank * m * nl * 2 if layout == "blocks" else rank * nl * 2
+        assert dests == [gather.addrs[call % 2][r] + offset for r in order]
+        assert dests[0] - gather.addrs[call % 2][rank] == offset
+    assert gather.ld == (nl if layout == "blocks" else n)
+    assert len(handles_seen) == 1 and len(handles_seen[0]) == 2
+    gather.outputs = []
+    gather.close()
+    for addr in others:
+        peers.free(addr)
+    assert not peers.segments
