@@ -287,3 +287,37 @@ def test_peer_column_gather_destinations_at_eight_ranks(monkeypatch, layout):
     for addr in others:
         peers.free(addr)
     assert not peers.segments
+
+
+def test_shard_plans_partition_and_repack_exactly():
+    """Property check over many sizes: row ranges tile [0, total) in rank order
+    with sizes differing by at most one, and the per-rank packed gate/up shards
+    hold exactly the packed weight's rows (gate block, then up block)."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    @settings(max_examples=200, deadline=None)
+    @given(total=st.integers(0, 5000), world=st.integers(1, 8))
+    def ranges(total, world):
+        spans = [sharding.shard_range(total, r, world) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == total
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        sizes = [hi - lo for lo, hi in spans]
+        assert max(sizes) - min(sizes) <= 1
+
+    @settings(max_examples=100, deadline=None)
+    @given(n=st.integers(1, 40), k=st.integers(1, 5), world=st.integers(1, 8))
+    def repack(n, k, world):
+        packed = torch.arange(2 * n * k, dtype=torch.float32).view(2 * n, k)
+        gates, ups = [], []
+        for r in range(world):
+            shard = sharding.pack_gate_up_shard(packed, r, world)
+            lo, hi = sharding.shard_range(n, r, world)
+            assert shard.shape == (2 * (hi - lo), k)
+            gates.append(shard[: hi - lo])
+            ups.append(shard[hi - lo:])
+        assert torch.equal(torch.cat(gates), packed[:n])
+        assert torch.equal(torch.cat(ups), packed[n:])
+
+    ranges()
+    repack()
