@@ -43,3 +43,9 @@ def test_reference_arm_is_silent_on_other_ranks():
                           "--gpus", "2", "--steps", "1", "--warmup", "3"], cwd=ROOT, env=env,
                          capture_output=True, text=True, timeout=300, check=True)
     assert out.stdout.strip() == ""
+
+
+def test_bench_rejects_fewer_than_three_warmup_steps():
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--warmup", "2"], cwd=ROOT,
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 2 and "--warmup must be >= 3" in out.stderr
