@@ -249,9 +249,14 @@ int reduce_with_pool_scratch(const float* x, void* out, std::uint64_t n, cudaStr
 // every host thread) use the stream-ordered pool path.
 constexpr int kMaxStreamScratch = 256;
 
+// Entries are keyed by the stream's process-unique id (cudaStreamGetId), not
+// by its handle: a destroyed stream's handle value may be reused for a new
+// stream, which must not inherit the old stream's block while work of the
+// old one could still be pending.  A block is never freed; it lives until
+// the process exits (at most kMaxStreamScratch of them).
 struct StreamScratch {
   int device;
-  cudaStream_t stream;
+  unsigned long long stream_id;
   double* partials;
   unsigned* counter;
 };
@@ -332,9 +337,14 @@ bool stream_scratch(cudaStream_t s, unsigned ctas, double** partials, unsigned**
     std::lock_guard<std::mutex> lock(capture_mu);
     make_capture_blocks(dev, capacity, s);
   }
+  unsigned long long id = 0;
+  if (cudaStreamGetId(s, &id) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < used; ++i) {
-    if (entries[i].device == dev && entries[i].stream == s) {
+    if (entries[i].device == dev && entries[i].stream_id == id) {
       *partials = entries[i].partials;
       *counter = entries[i].counter;
       return true;
@@ -354,7 +364,7 @@ bool stream_scratch(cudaStream_t s, unsigned ctas, double** partials, unsigned**
     cudaFree(block);
     return false;
   }
-  entries[used++] = StreamScratch{dev, s, p, c};
+  entries[used++] = StreamScratch{dev, id, p, c};
   *partials = p;
   *counter = c;
   return true;

@@ -126,10 +126,12 @@ class _Library:
             )
         self.path = path
         self.handle = ctypes.CDLL(str(path))
+        self.functions: dict[str, Callable] = {}
         for name in symbols if symbols is not None else tuple(_SIGNATURES):
             function = getattr(self.handle, name)
             function.argtypes = _SIGNATURES[name]
             function.restype = _RESTYPES.get(name, ctypes.c_int)
+            self.functions[name] = function
 
     def check(self, code: int) -> None:
         if code == 0:
@@ -154,17 +156,32 @@ def library_path() -> Path:
     return _default_library_path()
 
 
-def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
-    return ctypes.c_void_p(t.data_ptr())
+# The per-call host path is kept short (a single GEMM call is launch-bound):
+# pointers and sizes go to ctypes as plain ints (the declared argtypes convert
+# them), the current stream is read as a raw handle without building a
+# torch.cuda.Stream object, and each symbol's function object is looked up
+# once and kept.
+try:
+    from torch._C import _cuda_getCurrentRawStream as _raw_stream
+except ImportError:  # pragma: no cover - older torch
+    _raw_stream = None
 
 
-def _stream(t: torch.Tensor) -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream(device=t.device).cuda_stream)
+def _ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(t.get_device())
+    return torch.cuda.current_stream(device=t.device).cuda_stream
 
 
 def _call(symbol: str, *args) -> None:
-    library = _library()
-    library.check(getattr(library.handle, symbol)(*args))
+    library = _LIBRARY if _LIBRARY is not None else _library()
+    code = library.functions[symbol](*args)
+    if code:
+        library.check(code)
 
 
 def _export(name: str, fn: Callable, doc: str) -> Callable:

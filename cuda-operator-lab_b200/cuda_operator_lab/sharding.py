@@ -1,6 +1,6 @@
 """Multi-GPU partitioning of the large workloads (one process per GPU).
 
-The reference is single-GPU; these helpers add the BASELINE sharding plan:
+The reference is single-GPU; these helpers add a sharding plan for one box:
 
 * row-wise ops (norms, softmax, pointwise) split rows into contiguous ranges,
   one per rank, with no exchange;
@@ -262,7 +262,14 @@ class PeerColumnGather:
                  row_scale: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's GEMM (packed_shard [2N/g, K], optional row scale) and the
         gather; returns the output holding every rank's block ([g, M, N/g] or
-        [M, N], see ``layout``)."""
+        [M, N], see ``layout``).
+
+        The barrier that completes the gather waits a bounded time
+        (``peers.timeout_ns``); when it gives up, the returned buffer may miss
+        other ranks' blocks and nothing is raised here, because the host never
+        waits for the device.  Call :meth:`check` (it synchronises) before
+        trusting an output: it raises if any barrier since the last check
+        timed out."""
         if x.shape[0] != self.m or packed_shard.shape[0] != 2 * self.n_local:
             raise ValueError(f"expected x[{self.m}, K] and a packed shard of "
                              f"{2 * self.n_local} rows")
@@ -271,6 +278,15 @@ class PeerColumnGather:
         self.peers.gemm(x, row_scale, packed_shard, self.destinations(call), self.ld)
         self.peers.barrier(self.flag_addrs, self.rank, self.calls)
         return self.outputs[call % 2]
+
+    def check(self) -> None:
+        """Raise RuntimeError if a peer barrier of an earlier call gave up
+        waiting (its output may lack other ranks' blocks).  Synchronises the
+        device and clears the status word."""
+        code = self.peers.status()
+        if code != 0:
+            raise RuntimeError(f"fused all-gather: a peer barrier timed out (status {code}); "
+                               "outputs since the last check may miss other ranks' blocks")
 
     def close(self) -> None:
         """Unmaps the peers' buffers and frees this rank's (collective).  Output

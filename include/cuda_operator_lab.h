@@ -26,7 +26,8 @@
  * reference's shape guards (gemm_swiglu.cu:1125,1169,1213,1257).
  *
  * The second block holds entry points the reference does not have; each
- * names the BASELINE workload or the multi-GPU step it serves.
+ * names the workload (bf16 norms and GEMMs of a Llama-style MLP block) or the
+ * multi-GPU step it serves.
  */
 #ifndef CUDA_OPERATOR_LAB_H_
 #define CUDA_OPERATOR_LAB_H_
@@ -49,9 +50,13 @@ extern "C" {
  * its stream once).  A call captured into a CUDA graph takes one of those
  * reserved blocks for good, never the stream's; beyond them, and for
  * cudaStreamPerThread, the scratch is a stream-ordered allocation from a
- * library-owned cudaMemPool (graph memory nodes under capture).  A stream
- * handle must not be destroyed and re-created (same value) while the old
- * stream still has a reduction in flight. */
+ * library-owned cudaMemPool (graph memory nodes under capture).  Per-stream
+ * blocks are keyed by the stream's unique id (cudaStreamGetId), so a new
+ * stream never inherits a destroyed stream's block; blocks are never freed
+ * and live until the process exits (at most 256).  A captured call keeps its
+ * block in the graph: replays of one captured reduction (the same graph exec
+ * launched on two streams at once, or two instantiations of the same
+ * captured graph run concurrently) share it and must not overlap on the GPU. */
 int cuda_operator_reduction_v0(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:8  */
 int cuda_operator_reduction_v1(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:14 */
 int cuda_operator_reduction_v2(const float* input, float* output, uint64_t n, void* stream); /* reduction.cuh:20 */
@@ -254,9 +259,12 @@ int cuda_operator_reduction_partial_f64(const float* input, double* partial, uin
  * reference: it is for callers that cannot let a library allocate (a server
  * that reserved the whole device for its own allocator at start-up, a host
  * whose plugins must not allocate, a loop where an allocator call could
- * synchronise).  Same result contract as cuda_operator_reduction_v*, computed
- * by the same kernel, with its scratch in a fixed 128 KiB array inside the
- * library image (held by every GPU that loads the library until exit).
+ * synchronise).  Same kernel and accuracy as cuda_operator_reduction_v*
+ * (fp64 accumulation, fixed combine order, bit-reproducible run to run), but
+ * it splits the input into fixed 16384-element chunks rather than one wave
+ * of CTAs, so its result may differ from cuda_operator_reduction_v* in the
+ * last bits.  Its scratch is a fixed 128 KiB array inside the library image
+ * (held by every GPU that loads the library until exit).
  * Accepts n <= 268435456 (2^28); larger n returns 10004 before any launch.
  * All calls on a device share that array: calls whose GPU work overlaps
  * (unordered streams) race; calls ordered on one stream are safe.  Each call

@@ -10,12 +10,15 @@ copy, no CMake: plain nvcc, the same flags for every file) and links them into
 ``cuda_operator_*`` symbols.  Its cuBLAS/cuBLASLt versions dlopen the CUDA
 libraries at run time, as the reference does.
 
-Usage: python oracle/build_ref.py [/path/to/reference]
+Usage: python oracle/build_ref.py [/path/to/reference]; without an argument the
+checkout is taken from ``$COL_REFERENCE_DIR``, else from ``reference/`` beside
+this repository.
 """
 
 from __future__ import annotations
 
 import concurrent.futures
+import os
 import shutil
 import subprocess
 import sys
@@ -27,7 +30,16 @@ LIB = OUT_DIR / "libcuda_operator_lab_ref.so"
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-Xcompiler", "-fPIC"]
 
 
-def build(reference_root: Path = Path("/root/reference")) -> Path | None:
+def default_reference_root() -> Path:
+    """The reference checkout: ``$COL_REFERENCE_DIR`` or ``../reference``
+    relative to the repository root."""
+    override = os.environ.get("COL_REFERENCE_DIR")
+    return Path(override) if override else HERE.parent.parent / "reference"
+
+
+def build(reference_root: Path | None = None) -> Path | None:
+    if reference_root is None:
+        reference_root = default_reference_root()
     sources = sorted((reference_root / "csrc").glob("*/*.cu"))
     if not sources:
         return None
@@ -57,5 +69,5 @@ def build(reference_root: Path = Path("/root/reference")) -> Path | None:
 
 
 if __name__ == "__main__":
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    root = Path(sys.argv[1]) if len(sys.argv) > 1 else default_reference_root()
     print(build(root))

@@ -5,7 +5,7 @@ to run the tests): imports ``python/cuda_operator_lab/references.py`` of the
 reference by path, evaluates each of its functions on small seeded CPU inputs
 that cover the edge cases the reference's tests exercise (single elements,
 widths around warp/vector boundaries, odd widths, +-1000 logits, large-offset
-LayerNorm rows, a K=64 GEMM in the shape family of the BASELINE small config), and saves inputs and outputs.
+LayerNorm rows, a K=64 GEMM in the shape family of the small benchmark GEMM), and saves inputs and outputs.
 
 Usage: python tests/golden/make_golden.py /path/to/reference
 """

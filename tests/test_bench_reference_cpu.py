@@ -49,3 +49,47 @@ def test_bench_rejects_fewer_than_three_warmup_steps():
     out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--warmup", "2"], cwd=ROOT,
                          capture_output=True, text=True, timeout=300)
     assert out.returncode == 2 and "--warmup must be >= 3" in out.stderr
+
+
+def _bench_module():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("col_bench", ROOT / "bench.py")
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    return module
+
+
+def test_parity_check_flags_a_planted_error():
+    """The benchmark's parity block: identical rows pass; one element moved
+    past the bf16 bar (2e-2 + 2e-2 |expected|) is counted as a violation."""
+    import torch
+
+    bench = _bench_module()
+    g = torch.Generator()
+    g.manual_seed(11)
+    expected = torch.randn(8, 64, generator=g).to(torch.bfloat16)
+    same = bench.parity_check(expected.clone(), expected, 8)
+    assert same["ok"] and same["violations"] == 0 and same["max_abs_err"] == 0.0
+    planted = expected.clone()
+    planted[3, 7] = float(expected[3, 7]) + 0.05 + 0.05 * abs(float(expected[3, 7]))
+    bad = bench.parity_check(planted, expected, 8)
+    assert not bad["ok"] and bad["violations"] == 1 and bad["max_err_over_bound"] > 1.0
+
+
+def test_benchmark_inputs_are_shared_by_every_arm_and_shard():
+    """Each rank's packed shard holds exactly its gate and up rows of the one
+    seeded W that the CPU arms use (checked on a reduced N for speed)."""
+    import torch
+
+    bench = _bench_module()
+    bench.M, bench.K, bench.N = 64, 32, 96
+    full = bench.make_inputs(1, 0, "cpu")
+    for world in (2, 4):
+        for rank in range(world):
+            part = bench.make_inputs(world, rank, "cpu")
+            nl = 96 // world
+            assert torch.equal(part["x"], full["x"]) and torch.equal(part["w_norm"], full["w_norm"])
+            gate = full["packed"][rank * nl:(rank + 1) * nl]
+            up = full["packed"][96 + rank * nl:96 + (rank + 1) * nl]
+            assert torch.equal(part["packed"], torch.cat((gate, up)))

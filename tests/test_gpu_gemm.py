@@ -4,10 +4,10 @@ bf16 operands run on the tcgen05 tensor-core kernel (TMA-addressable shapes)
 or the CUDA-core kernel (K not a multiple of 8); fp32 operands run on the same
 tensor-core kernel through a three-part bf16 split (m*n*k >= 4e6) or on the
 CUDA-core kernel (smaller problems).  Tolerances: bf16 epilogues rtol 2e-2 / atol 2e-2 against
-the fp32-accumulated reference (BASELINE), fp32 epilogues rtol/atol 3e-4
+the fp32-accumulated reference (the project's bf16 bar), fp32 epilogues rtol/atol 3e-4
 (reference tests/test_gemm_bias_gelu_v0.py).  Shapes follow the reference's
 tests (tests/test_gemm_swiglu_v4.py:16-28, test_gemm_swiglu_v11.py:19-31)
-plus tile-boundary and BASELINE shapes.
+plus tile-boundary and benchmark-workload shapes.
 """
 
 from __future__ import annotations
@@ -227,7 +227,12 @@ def test_rmsnorm_folded_into_gemm_swiglu(m, k, n):
     torch.testing.assert_close(rstd.cpu(), oracle.rmsnorm_rstd(x, 1e-6), rtol=1e-5, atol=1e-7)
     actual = b.gemm_swiglu_rowscale_bf16(xd, rstd, folded.to(DEV))
     close(actual, oracle.gemm_swiglu_rowscale_bf16(x, rstd.cpu(), folded), BF_RTOL, BF_ATOL)
-    # and the unfused block it replaces: RMSNorm (bf16) then the packed GEMM+SwiGLU
+    # Against the unfused block (RMSNorm to bf16, then the packed GEMM+SwiGLU)
+    # the folded form agrees within 3e-2, not the 2e-2 bar: its one bf16
+    # rounding falls on W * w instead of on the normalised X, and at the 2e-2
+    # bar a few elements in a million differ by more (a CPU emulation of both
+    # on 4M outputs: max 1.34x the bound).  The benchmark's headline step is
+    # therefore the unfused block, pinned at 2e-2 in test_gpu_headline.py.
     unfused = oracle.gemm_swiglu_bf16_fp32_reference(oracle.rmsnorm_bf16(x, w_norm, 1e-6), packed)
     close(actual, unfused, 3e-2, 3e-2)
 

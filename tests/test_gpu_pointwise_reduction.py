@@ -2,7 +2,7 @@
 
 Reduction sizes follow the reference (tests/test_reduction_v5.py:16-44): 0,
 1, around warp/block/vector boundaries, the 524287/524288/524289 dispatch
-thresholds and an odd 1,000,003, plus the BASELINE 16,777,216 and a
+thresholds and an odd 1,000,003, plus the benchmark's 16,777,216 and a
 ~2^28-element case checked against a float64 sum (relative error <= 1e-6).
 """
 
@@ -36,7 +36,7 @@ def test_bias_gelu_matches_oracle(version, rows, cols):
     bias = torch.randn(cols, generator=g) * 0.1
     fn = getattr(b, f"fused_bias_gelu_v{version}")
     actual = fn(x.to(DEV), bias.to(DEV))
-    # BASELINE bar against the exact function of the fp32 inputs.  PyTorch's
+    # the fp32 bar (rtol 1e-5 / atol 1e-6) against the exact function of the fp32 inputs.  PyTorch's
     # own fp32 CPU GELU is off by up to 1.2e-6 near |z| = 3.5, so against the
     # reference's CPU path the reference tests' bar (5e-6) applies.
     exact = torch.nn.functional.gelu((x + bias).double()).float()
@@ -68,7 +68,7 @@ def test_pointwise_unaligned_views():
     close(b.swiglu_v1(gate, up), oracle.swiglu(gate.cpu(), up.cpu()))
     bias = torch.randn(4096, generator=g).to(DEV)
     actual = b.fused_bias_gelu_v1(gate, bias)
-    # as in test_bias_gelu_matches_oracle: BASELINE bar against the exact
+    # as in test_bias_gelu_matches_oracle: the fp32 bar against the exact
     # function, the reference tests' bar against PyTorch's fp32 CPU GELU
     exact = torch.nn.functional.gelu((gate.cpu() + bias.cpu()).double()).float()
     close(actual, exact)

@@ -5,8 +5,8 @@ outputs (GPU).
 Shapes follow the reference's tests (tests/test_rmsnorm_v0.py:16-32,
 tests/test_softmax_v2.py:16-41): empty, single element, widths around the
 warp (31/32/33) and vector boundaries, odd widths (4097, 8193), the
-BASELINE shapes and rows wider than the register path (the streaming
-kernel).  Tolerance: BASELINE's fp32 bar, rtol 1e-5 / atol 1e-6.
+benchmark-workload shapes and rows wider than the register path (the streaming
+kernel).  Tolerance: the fp32 bar, rtol 1e-5 / atol 1e-6.
 """
 
 from __future__ import annotations

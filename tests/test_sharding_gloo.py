@@ -229,6 +229,38 @@ def test_peer_column_gather_rejects_bad_shapes():
     assert not peers.segments
 
 
+def test_peer_column_gather_check_raises_after_a_barrier_timeout():
+    """A barrier that gave up leaves a non-zero status word: check() turns it
+    into an error (and passes when every barrier completed)."""
+
+    class TimedOutPeers(HostPeers):
+        def __init__(self) -> None:
+            super().__init__()
+            self.code = 0
+
+        def barrier(self, flag_addrs, rank, epoch) -> None:
+            pass  # one rank: nothing to wait for
+
+        def status(self) -> int:
+            code, self.code = self.code, 0
+            return code
+
+    peers = TimedOutPeers()
+    gather = sharding.PeerColumnGather(8, 20, peers=peers)
+    g = torch.Generator()
+    g.manual_seed(7)
+    x = torch.randn(8, 16, generator=g).to(torch.bfloat16)
+    packed = torch.randn(40, 16, generator=g).to(torch.bfloat16)
+    gather(x, packed, torch.ones(8))
+    gather.check()
+    peers.code = 2  # bit 1: the wait for a peer's flag ran out
+    with pytest.raises(RuntimeError, match="timed out"):
+        gather.check()
+    gather.check()  # the status word was cleared by the failing check
+    gather.close()
+    assert not peers.segments
+
+
 def test_peer_column_gather_releases_memory_when_setup_fails():
     class FailingPeers(HostPeers):
         def __init__(self) -> None:
@@ -293,8 +325,8 @@ def test_shard_plans_partition_and_repack_exactly():
     """Property check over many sizes: row ranges tile [0, total) in rank order
     with sizes differing by at most one, and the per-rank packed gate/up shards
     hold exactly the packed weight's rows (gate block, then up block)."""
-    from hypothesis import given, settings
-    from hypothesis import strategies as st
+    hypothesis = pytest.importorskip("hypothesis")
+    given, settings, st = hypothesis.given, hypothesis.settings, hypothesis.strategies
 
     @settings(max_examples=200, deadline=None)
     @given(total=st.integers(0, 5000), world=st.integers(1, 8))
