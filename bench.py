@@ -529,9 +529,14 @@ def run_ours(args, d: Dist) -> dict | None:
     # as soon as the GEMM two steps back has read its buffer, so it overlaps
     # the previous GEMM's last, partly idle wave of tiles; step i's GEMM waits
     # for it.  Every step's RMSNorm and GEMM run inside the timed region.
+    # The GEMM's stream has the higher priority: when both kernels are ready,
+    # the block scheduler places the GEMM's CTAs first, and the RMSNorm's take
+    # the SMs that the GEMM's last wave leaves idle (without priorities the
+    # RMSNorm could take SMs at the GEMM's start and delay its persistent CTAs).
     # CUDA events around every GEMM launch of the timed steps (on the
     # launching stream) give the dominant kernel's average duration.
-    main = torch.cuda.current_stream()
+    main = torch.cuda.Stream(priority=-1)
+    main.wait_stream(torch.cuda.current_stream())
     side = torch.cuda.Stream()
     xns = [torch.empty_like(x) for _ in range(2)]
     normed = [torch.cuda.Event() for _ in range(2)]
@@ -564,8 +569,9 @@ def run_ours(args, d: Dist) -> dict | None:
 
     b.gemm_status(clear=True)
     gpus = list(range(d.world))
-    with ClockSampler(gpus) as clocks:
+    with ClockSampler(gpus) as clocks, torch.cuda.stream(main):
         ms = time_region(d, step, args.steps, args.warmup, drain=drain, after_start=start)
+    torch.cuda.current_stream().wait_stream(main)
     gemm_us = d.max(1000.0 * sum(s_.elapsed_time(e_) for s_, e_ in gemm_events) / args.steps)
     clock_info = clocks.summary() if d.rank == 0 else None
     status = b.gemm_status(clear=True)
@@ -995,7 +1001,8 @@ def run_reference(args) -> dict:
 
 
 KERNEL_CASES = ("gemm_swiglu_bf16", "gemm_bias_gelu_bf16", "rmsnorm_bf16", "reduction",
-                "rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "bias_gelu_fp32", "swiglu_fp32",
+                "rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "residual_layernorm_fp32",
+                "bias_gelu_fp32", "swiglu_fp32",
                 "gemm_bias_gelu_fp32", "gemm_swiglu_fp32", "residual_rmsnorm_bf16",
                 "gemm_residual_bf16", "gemm_swiglu_rowscale_bf16")
 
@@ -1060,8 +1067,8 @@ def run_kernel_case(spec: str, reps: int, timed: bool = False) -> None:
         x = torch.rand(n, device=dev, generator=g) * 2 - 1
         out = torch.empty(1, device=dev)
         fn = lambda: b.reduction_v5_into(x, out)  # noqa: E731
-    elif name in ("rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "bias_gelu_fp32",
-                  "swiglu_fp32"):
+    elif name in ("rmsnorm_fp32", "softmax_fp32", "layernorm_fp32", "residual_layernorm_fp32",
+                  "bias_gelu_fp32", "swiglu_fp32"):
         r, c = d or (128, 8192 if name == "rmsnorm_fp32" else 4096)
         x, w, bias, y = rn(r, c), torch.rand(c, device=dev, generator=g) + 0.5, rn(c) * 0.1, None
         y = torch.empty_like(x)
@@ -1069,6 +1076,8 @@ def run_kernel_case(spec: str, reps: int, timed: bool = False) -> None:
         fn = {"rmsnorm_fp32": lambda: b.rmsnorm_v4_into(x, w, y, EPS),
               "softmax_fp32": lambda: b.softmax_v5_into(x, y),
               "layernorm_fp32": lambda: b.layernorm_v5_into(x, w, bias, y),
+              "residual_layernorm_fp32": lambda: b.fused_residual_layernorm_v4_into(x, u, w, bias,
+                                                                                    y),
               "bias_gelu_fp32": lambda: b.fused_bias_gelu_v2_into(x, bias, y),
               "swiglu_fp32": lambda: b.swiglu_v2_into(x, u, y)}[name]
     if not timed:

@@ -12,6 +12,7 @@
 #include "gemm_simt.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_2sm.cuh"
+#include "gemm_sm100_sk.cuh"
 
 namespace {
 
@@ -144,6 +145,36 @@ int set_smem_attr_2sm(int dev) {
   return 0;
 }
 
+// Split-K cluster kernel (gemm_sm100_sk.cuh): shared-memory attribute and the
+// number of co-resident 4-CTA clusters, both once per device.
+template <int EPI, typename TOut>
+int sk_clusters(int dev) {
+  static int cached[64] = {};
+  static std::once_flag flags[64];
+  std::call_once(flags[dev & 63], [dev]() {
+    auto kernel = col::sm100::gemm_bf16_sk_kernel<EPI, TOut>;
+    int clusters = 0;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(col::sm100::kSkSmemBytes)) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(4, 1, 1);
+      cfg.blockDim = dim3(col::sm100::kCtaThreads, 1, 1);
+      cfg.dynamicSmemBytes = col::sm100::kSkSmemBytes;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 4;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) clusters = 0;
+    }
+    cudaGetLastError();  // a failed query means: no split-K path
+    cached[dev & 63] = clusters > 0 ? clusters : 0;
+  });
+  return cached[dev & 63];
+}
+
 enum class BMode { kSwiGLU, kGelu };
 
 // Tile width: the B box height BNH (MMA N = 2*BNH; output columns per tile =
@@ -161,7 +192,7 @@ constexpr std::uint64_t kKBlockFloor = 1365;
 constexpr int kNarrowMaxKBlocks = 16;
 
 int choose_bnh(int mblocks, std::uint64_t n, bool swiglu, int sm_count, int max_bnh,
-               bool with112, bool with32) {
+               bool with112, bool with32, std::uint64_t* cost_out = nullptr) {
   constexpr int kCandidates[] = {128, 112, 96, 64, 32};
   int best = 64;
   std::uint64_t best_cost = ~0ull;
@@ -176,8 +207,18 @@ int choose_bnh(int mblocks, std::uint64_t n, bool swiglu, int sm_count, int max_
       best = bnh;
     }
   }
+  if (cost_out) *cost_out = best_cost;
   return best;
 }
+
+// Split-K cluster path (gemm_sm100_sk.cuh) for GELU-form GEMMs (bias+GELU,
+// residual): one 256x256 tile per cluster of two CTA pairs, each pair half of
+// K.  Chosen when every tile has a cluster (one wave) and the cost model --
+// per-k-block floor as in choose_bnh, half the k-blocks at MMA N = 256, plus
+// the partial-accumulator exchange counted as kSkExchangeKBlocks k-blocks --
+// beats the best one-pair-per-tile choice.  Needs K long enough to split.
+constexpr int kSkMinKBlocks = 16;
+constexpr std::uint64_t kSkExchangeKBlocks = 3;
 
 // fp32 emulation (below): k-blocks per flushed accumulation chunk of the a0*b0 segment (512 k): on
 // unit-scale data the max error against a float64 GEMM is ~5e-8 of
@@ -259,8 +300,49 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
   // BNH = 32 (twice the tiles of 64, each with half the B box and half the
   // epilogue) only where a tile's fixed cost outweighs its main loop.
   const bool with32 = !FLUSH && ops.k_blocks <= kNarrowMaxKBlocks;
+  std::uint64_t tile_cost = 0;
   const int bnh = choose_bnh(mblocks_sched, n, mode == BMode::kSwiGLU,
-                             use_pair ? pair_slots : info.sm_count, max_bnh, !FLUSH, with32);
+                             use_pair ? pair_slots : info.sm_count, max_bnh, !FLUSH, with32,
+                             &tile_cost);
+  if constexpr (!FLUSH && (EPI == col::sm100::kEpiBiasGeluErf ||
+                           EPI == col::sm100::kEpiBiasGeluTanh || EPI == col::sm100::kEpiResidual)) {
+    if (use_pair && gather == nullptr && ops.seg_k_blocks == 0 && mode == BMode::kGelu &&
+        ops.k_blocks >= kSkMinKBlocks) {
+      const std::uint64_t sk_nblocks = (n + 255) / 256;
+      const std::uint64_t sk_tiles = static_cast<std::uint64_t>(mblocks_sched) * sk_nblocks;
+      const int clusters = sk_clusters<EPI, TOut>(dev);
+      const std::uint64_t kb = static_cast<std::uint64_t>(ops.k_blocks);
+      const std::uint64_t sk_cost = ((kb + 1) / 2 + kSkExchangeKBlocks) * (kKBlockFloor + 256);
+      if (clusters > 0 && sk_tiles <= static_cast<std::uint64_t>(clusters) &&
+          sk_cost < tile_cost * kb) {
+        GemmParams p;
+        std::memset(&p, 0, sizeof(p));
+        int rc = encode_bf16_rows(&p.map_a, ops.a, m, ops.a_cols, 128);
+        if (rc == 0) rc = encode_bf16_rows(&p.map_b0, ops.b0, ops.b_rows, ops.b_cols, 128);
+        if (rc == col::kErrTensorMapEncode) return -1;
+        if (rc != 0) return rc;
+        p.map_b1 = p.map_b0;
+        p.bias = bias;
+        p.residual = residual;
+        p.out = out;
+        p.status = status;
+        p.m = static_cast<int>(m);
+        p.n = static_cast<int>(n);
+        p.k = static_cast<int>(ops.a_cols);
+        p.num_m_blocks = mblocks_sched;
+        p.num_n_blocks = static_cast<int>(sk_nblocks);
+        p.num_k_blocks = ops.k_blocks;
+        p.b_row_stride = 256;
+        p.b1_row_offset = 128;
+        p.out_ld = static_cast<int>(n);
+        p.out_vec_ok = col::aligned16(out) && ((n * sizeof(TOut)) % 16 == 0);
+        return col::launch_serialised(col::sm100::gemm_bf16_sk_kernel<EPI, TOut>,
+                                      dim3(static_cast<unsigned>(4 * sk_tiles)),
+                                      dim3(col::sm100::kCtaThreads),
+                                      col::sm100::kSkSmemBytes, s, p);
+      }
+    }
+  }
 
   GemmParams p;
   std::memset(&p, 0, sizeof(p));

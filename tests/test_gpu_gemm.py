@@ -109,8 +109,14 @@ def test_gemm_swiglu_bf16_output(m, k, n):
     close(actual, oracle.gemm_swiglu_bf16_fp32_reference(x, packed), BF_RTOL, BF_ATOL)
 
 
+# (512, 4096, 4096), (300, 2048, 1000), (512, 1024, 4096), (256, 8192, 512) and
+# (768, 4096, 2048) run the split-K cluster kernel (two CTA pairs per tile,
+# each half of K, partial accumulator exchanged through distributed shared
+# memory), the others one CTA (pair) per tile
 @pytest.mark.parametrize(("m", "k", "n"), [(1, 8, 1), (16, 64, 64), (100, 256, 300),
-                                           (512, 4096, 4096), (257, 520, 1000), (3, 30, 5)])
+                                           (512, 4096, 4096), (257, 520, 1000), (3, 30, 5),
+                                           (300, 2048, 1000), (512, 1024, 4096),
+                                           (256, 8192, 512), (768, 4096, 2048)])
 def test_gemm_bias_gelu_bf16(m, k, n):
     g = seeded(20261202 + m + k + n)
     x = torch.randn(m, k, generator=g).to(torch.bfloat16)
@@ -191,7 +197,7 @@ def test_long_k_few_tiles(m, k, n):
 
 @pytest.mark.parametrize(("m", "k", "n"), [(1, 8, 1), (16, 64, 64), (100, 256, 300),
                                            (512, 14336, 4096), (257, 520, 1000), (3, 30, 5),
-                                           (1024, 4096, 4096)])
+                                           (1024, 4096, 4096), (300, 2048, 1000)])
 def test_gemm_residual_bf16(m, k, n):
     g = seeded(20261210 + m + k + n)
     x = torch.randn(m, k, generator=g).to(torch.bfloat16)
@@ -289,6 +295,17 @@ def test_packed_versions_agree_bit_for_bit():
     v4, v10, v11 = (getattr(b, f"gemm_swiglu_v{v}")(xd, packed) for v in (4, 10, 11))
     torch.cuda.synchronize()
     assert torch.equal(v10, v11) and torch.equal(v4, v11)
+
+
+def test_split_k_gemm_is_bitwise_stable():
+    # the split-K cluster kernel adds the two halves of K in a fixed order
+    g = seeded(78)
+    x = torch.randn(512, 4096, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(4096, 4096, generator=g) * 4096 ** -0.5).to(torch.bfloat16).to(DEV)
+    bias = (torch.randn(4096, generator=g) * 0.1).to(DEV)
+    first = b.gemm_bias_gelu_bf16(x, w, bias)
+    for _ in range(3):
+        assert torch.equal(b.gemm_bias_gelu_bf16(x, w, bias), first)
 
 
 def test_gemm_repeated_calls_are_bitwise_stable():

@@ -71,8 +71,10 @@ def no_wait_timeouts():
     assert b.gemm_status(clear=True) == 0
 
 
+# (300, 2048, 1000) and (384, 1024, 264) take the split-K cluster kernel for
+# bias+GELU and the residual GEMM
 GEMM_SHAPES = [(129, 72, 130), (1000, 520, 700), (257, 520, 1000), (1, 8, 1), (128, 64, 2048),
-               (384, 1024, 264)]
+               (384, 1024, 264), (300, 2048, 1000)]
 
 
 @pytest.mark.parametrize("offset", [0, 1])
