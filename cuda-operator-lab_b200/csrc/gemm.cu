@@ -49,10 +49,33 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+// Recently encoded tensor maps of the calling thread.  A map is a pure
+// function of (base, rows, cols, box_rows) -- the element type, swizzle, L2
+// promotion and fill are fixed -- so a call on the same operands (the common
+// case: weights, and activations in reused buffers) copies 128 bytes instead
+// of encoding again, which keeps a small GEMM's host path short.
+struct TensorMapCacheEntry {
+  CUtensorMap map;
+  const void* base;
+  std::uint64_t rows;
+  std::uint64_t cols;
+  std::uint32_t box_rows;
+  bool valid;
+};
+constexpr int kTensorMapCacheSize = 16;
+
 // 2-D bf16 map over a row-major [rows, cols] matrix; box = 64 columns (128 B,
 // the 128-byte swizzle span) x box_rows rows.  Out-of-range boxes read zeros.
 int encode_bf16_rows(CUtensorMap* map, const void* base, std::uint64_t rows, std::uint64_t cols,
                      std::uint32_t box_rows) {
+  thread_local TensorMapCacheEntry cache[kTensorMapCacheSize] = {};
+  const std::uintptr_t h = (reinterpret_cast<std::uintptr_t>(base) >> 7) ^ rows ^ (cols * 31u) ^
+                           (static_cast<std::uintptr_t>(box_rows) * 131u);
+  TensorMapCacheEntry& e = cache[(h ^ (h >> 4) ^ (h >> 9)) % kTensorMapCacheSize];
+  if (e.valid && e.base == base && e.rows == rows && e.cols == cols && e.box_rows == box_rows) {
+    std::memcpy(map, &e.map, sizeof(CUtensorMap));
+    return 0;
+  }
   auto enc = tensor_map_encoder();
   if (!enc) return col::kErrNoTensorMapEncoder;
   const cuuint64_t dims[2] = {cols, rows};
@@ -63,7 +86,14 @@ int encode_bf16_rows(CUtensorMap* map, const void* base, std::uint64_t rows, std
                          strides, box, estrides, CU_TENSOR_MAP_INTERLEAVE_NONE,
                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : col::kErrTensorMapEncode;
+  if (r != CUDA_SUCCESS) return col::kErrTensorMapEncode;
+  std::memcpy(&e.map, map, sizeof(CUtensorMap));
+  e.base = base;
+  e.rows = rows;
+  e.cols = cols;
+  e.box_rows = box_rows;
+  e.valid = true;
+  return 0;
 }
 
 template <int BNH, int EPI, typename TOut, bool FLUSH>

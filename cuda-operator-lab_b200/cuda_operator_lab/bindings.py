@@ -221,8 +221,8 @@ def _make_reduction(version: int) -> None:
     def into(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         _validate_reduction_input(x)
         _validate_reduction_output(x, out)
-        _call(symbol, _ptr(x) if x.numel() else ctypes.c_void_p(), _ptr(out),
-              ctypes.c_uint64(x.numel()), _stream(x))
+        _call(symbol, _ptr(x) if x.numel() else None, _ptr(out),
+              int(x.numel()), _stream(x))
         return out
 
     def alloc(x: torch.Tensor) -> torch.Tensor:
@@ -249,8 +249,8 @@ def reduction_partial_f64_into(x: torch.Tensor, out: torch.Tensor) -> torch.Tens
         raise ValueError("output must be a CUDA tensor on the same device")
     if out.dtype != torch.float64 or out.numel() != 1 or not out.is_contiguous():
         raise ValueError("output must be one contiguous float64 CUDA value")
-    _call("cuda_operator_reduction_partial_f64", _ptr(x) if x.numel() else ctypes.c_void_p(),
-          _ptr(out), ctypes.c_uint64(x.numel()), _stream(x))
+    _call("cuda_operator_reduction_partial_f64", _ptr(x) if x.numel() else None,
+          _ptr(out), int(x.numel()), _stream(x))
     return out
 
 
@@ -294,7 +294,7 @@ def _make_softmax(version: int) -> None:
         rows, cols = x.shape
         if rows == 0:
             return out
-        _call(symbol, _ptr(x), _ptr(out), ctypes.c_uint64(rows), ctypes.c_uint64(cols), _stream(x))
+        _call(symbol, _ptr(x), _ptr(out), int(rows), int(cols), _stream(x))
         return out
 
     def alloc(x: torch.Tensor) -> torch.Tensor:
@@ -351,8 +351,8 @@ def _make_rmsnorm(version: int) -> None:
         rows, cols = x.shape
         if rows == 0:
             return out
-        _call(symbol, _ptr(x), _ptr(weight), _ptr(out), ctypes.c_uint64(rows),
-              ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x))
+        _call(symbol, _ptr(x), _ptr(weight), _ptr(out), int(rows),
+              int(cols), float(eps), _stream(x))
         return out
 
     def alloc(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
@@ -375,8 +375,8 @@ def rmsnorm_bf16_into(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor,
     rows, cols = x.shape
     if rows == 0:
         return out
-    _call("cuda_operator_rmsnorm_bf16", _ptr(x), _ptr(weight), _ptr(out), ctypes.c_uint64(rows),
-          ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x))
+    _call("cuda_operator_rmsnorm_bf16", _ptr(x), _ptr(weight), _ptr(out), int(rows),
+          int(cols), float(eps), _stream(x))
     return out
 
 
@@ -409,7 +409,7 @@ def fused_residual_rmsnorm_into(x: torch.Tensor, residual: torch.Tensor, weight:
     symbol = ("cuda_operator_fused_residual_rmsnorm_bf16" if dtype == torch.bfloat16
               else "cuda_operator_fused_residual_rmsnorm_h")
     _call(symbol, _ptr(x), _ptr(residual), _ptr(weight), _ptr(h_out), _ptr(out),
-          ctypes.c_uint64(rows), ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x))
+          int(rows), int(cols), float(eps), _stream(x))
     return h_out, out
 
 
@@ -463,8 +463,8 @@ def _make_layernorm(version: int) -> None:
         rows, cols = x.shape
         if rows == 0:
             return out
-        _call(symbol, _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), ctypes.c_uint64(rows),
-              ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x))
+        _call(symbol, _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), int(rows),
+              int(cols), float(eps), _stream(x))
         return out
 
     def alloc(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
@@ -515,7 +515,7 @@ def _make_residual_layernorm(version: int) -> None:
         if rows == 0:
             return out
         _call(symbol, _ptr(x), _ptr(residual), _ptr(weight), _ptr(bias), _ptr(out),
-              ctypes.c_uint64(rows), ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x))
+              int(rows), int(cols), float(eps), _stream(x))
         return out
 
     def alloc(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
@@ -543,8 +543,8 @@ def fused_residual_layernorm_h_into(x: torch.Tensor, residual: torch.Tensor, wei
     if rows == 0:
         return h_out, out
     _call("cuda_operator_fused_residual_layernorm_h", _ptr(x), _ptr(residual), _ptr(weight),
-          _ptr(bias), _ptr(h_out), _ptr(out), ctypes.c_uint64(rows), ctypes.c_uint64(cols),
-          ctypes.c_float(eps), _stream(x))
+          _ptr(bias), _ptr(h_out), _ptr(out), int(rows), int(cols),
+          float(eps), _stream(x))
     return h_out, out
 
 
@@ -581,8 +581,8 @@ def _make_bias_gelu(version: int) -> None:
         rows, cols = x.shape
         if rows == 0:
             return out
-        _call(symbol, _ptr(x), _ptr(bias), _ptr(out), ctypes.c_uint64(rows),
-              ctypes.c_uint64(cols), _stream(x))
+        _call(symbol, _ptr(x), _ptr(bias), _ptr(out), int(rows),
+              int(cols), _stream(x))
         return out
 
     def alloc(x: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
@@ -622,12 +622,12 @@ def _make_swiglu(version: int) -> None:
             rows, cols = gate.shape
             if rows == 0:
                 return out
-            _call(symbol, _ptr(gate), _ptr(up), _ptr(out), ctypes.c_uint64(rows),
-                  ctypes.c_uint64(cols), _stream(gate))
+            _call(symbol, _ptr(gate), _ptr(up), _ptr(out), int(rows),
+                  int(cols), _stream(gate))
             return out
         if gate.numel() == 0:
             return out
-        _call(symbol, _ptr(gate), _ptr(up), _ptr(out), ctypes.c_uint64(gate.numel()),
+        _call(symbol, _ptr(gate), _ptr(up), _ptr(out), int(gate.numel()),
               _stream(gate))
         return out
 
@@ -670,8 +670,8 @@ def _make_gemm_bias_gelu(version: int) -> None:
         n = weight.shape[0]
         if m == 0 or n == 0:
             return out
-        _call(symbol, _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), ctypes.c_uint64(m),
-              ctypes.c_uint64(k), ctypes.c_uint64(n), _stream(x))
+        _call(symbol, _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), int(m),
+              int(k), int(n), _stream(x))
         return out
 
     def alloc(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
@@ -713,7 +713,7 @@ def gemm_bias_gelu_bf16_into(x_bf16: torch.Tensor, weight_bf16: torch.Tensor, bi
     if m == 0 or n == 0:
         return out_bf16
     _call("cuda_operator_gemm_bias_gelu_bf16", _ptr(x_bf16), _ptr(weight_bf16), _ptr(bias),
-          _ptr(out_bf16), ctypes.c_uint64(m), ctypes.c_uint64(k), ctypes.c_uint64(n),
+          _ptr(out_bf16), int(m), int(k), int(n),
           _stream(x_bf16))
     return out_bf16
 
@@ -757,8 +757,8 @@ def gemm_residual_bf16_into(x_bf16: torch.Tensor, weight_bf16: torch.Tensor,
     if k == 0:
         raise ValueError("GEMM residual requires k > 0")
     _call("cuda_operator_gemm_residual_bf16", _ptr(x_bf16), _ptr(weight_bf16),
-          _ptr(residual_bf16), _ptr(out_bf16), ctypes.c_uint64(m), ctypes.c_uint64(k),
-          ctypes.c_uint64(n), _stream(x_bf16))
+          _ptr(residual_bf16), _ptr(out_bf16), int(m), int(k),
+          int(n), _stream(x_bf16))
     return out_bf16
 
 
@@ -791,8 +791,8 @@ def rmsnorm_rstd_bf16_into(x_bf16: torch.Tensor, rstd: torch.Tensor,
     rows, cols = x_bf16.shape
     if rows == 0:
         return rstd
-    _call("cuda_operator_rmsnorm_rstd_bf16", _ptr(x_bf16), _ptr(rstd), ctypes.c_uint64(rows),
-          ctypes.c_uint64(cols), ctypes.c_float(eps), _stream(x_bf16))
+    _call("cuda_operator_rmsnorm_rstd_bf16", _ptr(x_bf16), _ptr(rstd), int(rows),
+          int(cols), float(eps), _stream(x_bf16))
     return rstd
 
 
@@ -838,8 +838,8 @@ def gemm_swiglu_rowscale_bf16_into(x_bf16: torch.Tensor, row_scale: torch.Tensor
     if m == 0 or n == 0:
         return out_bf16
     _call("cuda_operator_gemm_swiglu_rowscale_bf16", _ptr(x_bf16), _ptr(row_scale),
-          _ptr(packed_weight_bf16), _ptr(out_bf16), ctypes.c_uint64(m), ctypes.c_uint64(k),
-          ctypes.c_uint64(n), _stream(x_bf16))
+          _ptr(packed_weight_bf16), _ptr(out_bf16), int(m), int(k),
+          int(n), _stream(x_bf16))
     return out_bf16
 
 
@@ -891,9 +891,9 @@ def gemm_swiglu_allgather_bf16(x_bf16: torch.Tensor, row_scale: torch.Tensor | N
         return
     array = (ctypes.c_void_p * len(dests))(*[int(d) for d in dests])
     _call("cuda_operator_gemm_swiglu_allgather_bf16", _ptr(x_bf16),
-          _ptr(row_scale) if row_scale is not None else ctypes.c_void_p(),
-          _ptr(packed_weight_bf16), array, ctypes.c_int(len(dests)), ctypes.c_uint64(m),
-          ctypes.c_uint64(k), ctypes.c_uint64(n), ctypes.c_uint64(ld), _stream(x_bf16))
+          _ptr(row_scale) if row_scale is not None else None,
+          _ptr(packed_weight_bf16), array, int(len(dests)), int(m),
+          int(k), int(n), int(ld), _stream(x_bf16))
 
 
 def peer_alloc(nbytes: int) -> tuple[int, bytes]:
@@ -904,7 +904,7 @@ def peer_alloc(nbytes: int) -> tuple[int, bytes]:
     handle = ctypes.create_string_buffer(size)
     addr = ctypes.c_void_p()
     library.check(library.handle.cuda_operator_lab_peer_alloc(
-        ctypes.c_uint64(nbytes), ctypes.byref(addr), handle))
+        int(nbytes), ctypes.byref(addr), handle))
     return int(addr.value), handle.raw
 
 
@@ -937,8 +937,8 @@ def peer_barrier(flag_addrs: Sequence[int], rank: int, epoch: int,
         raise ValueError("need 1 <= world <= 8 and 0 <= rank < world")
     array = (ctypes.c_void_p * world)(*[int(a) for a in flag_addrs])
     s = stream if stream is not None else torch.cuda.current_stream()
-    _call("cuda_operator_lab_peer_barrier", array, ctypes.c_int(rank), ctypes.c_int(world),
-          ctypes.c_uint32(epoch & 0xFFFFFFFF), ctypes.c_uint64(timeout_ns),
+    _call("cuda_operator_lab_peer_barrier", array, int(rank), int(world),
+          int(epoch & 0xFFFFFFFF), int(timeout_ns),
           ctypes.c_void_p(s.cuda_stream))
 
 
@@ -946,7 +946,7 @@ def peer_status(clear: bool = True) -> int:
     """Peer status word of the current device (bit 1: a barrier wait timed out).
     Synchronises the device."""
     value = ctypes.c_uint(0)
-    _call("cuda_operator_lab_peer_status", ctypes.byref(value), ctypes.c_int(1 if clear else 0))
+    _call("cuda_operator_lab_peer_status", ctypes.byref(value), int(1 if clear else 0))
     return int(value.value)
 
 
@@ -985,7 +985,7 @@ def _make_gemm_swiglu_f32_dual(version: int) -> None:
         if workspace.data_ptr() == out.data_ptr():
             raise ValueError("workspace and output must not alias")
         _call(symbol, _ptr(x), _ptr(gate_weight), _ptr(up_weight), _ptr(workspace), _ptr(out),
-              ctypes.c_uint64(m), ctypes.c_uint64(k), ctypes.c_uint64(n), _stream(x))
+              int(m), int(k), int(n), _stream(x))
         return out
 
     def alloc(x: torch.Tensor, gate_weight: torch.Tensor, up_weight: torch.Tensor) -> torch.Tensor:
@@ -1049,7 +1049,7 @@ def _make_gemm_swiglu_packed(version: int, in_dtype: torch.dtype, ws_dtype: torc
         if m == 0 or n == 0:
             return out
         _call(symbol, _ptr(x), _ptr(packed_weight), _ptr(workspace), _ptr(out),
-              ctypes.c_uint64(m), ctypes.c_uint64(k), ctypes.c_uint64(n), _stream(x))
+              int(m), int(k), int(n), _stream(x))
         return out
 
     def alloc(x: torch.Tensor, packed_weight: torch.Tensor) -> torch.Tensor:
@@ -1104,7 +1104,7 @@ def _make_gemm_swiglu_bf16_dual(version: int) -> None:
         if (m % m_mult) != 0 or (k % k_mult) != 0 or (n % n_mult) != 0:
             raise ValueError(guard_message)
         _call(symbol, _ptr(x_bf16), _ptr(gate_weight_bf16), _ptr(up_weight_bf16), _ptr(out),
-              ctypes.c_uint64(m), ctypes.c_uint64(k), ctypes.c_uint64(n), _stream(x_bf16))
+              int(m), int(k), int(n), _stream(x_bf16))
         return out
 
     def alloc(x_bf16: torch.Tensor, gate_weight_bf16: torch.Tensor,
@@ -1165,7 +1165,7 @@ def gemm_swiglu_bf16_into(x_bf16: torch.Tensor, packed_weight_bf16: torch.Tensor
     if m == 0 or n == 0:
         return out_bf16
     _call("cuda_operator_gemm_swiglu_bf16", _ptr(x_bf16), _ptr(packed_weight_bf16), _ptr(out_bf16),
-          ctypes.c_uint64(m), ctypes.c_uint64(k), ctypes.c_uint64(n), _stream(x_bf16))
+          int(m), int(k), int(n), _stream(x_bf16))
     return out_bf16
 
 
@@ -1187,13 +1187,13 @@ def gemm_status(clear: bool = True) -> int:
     0 means no mbarrier wait ever ran out of time.  Synchronises the device.
     """
     value = ctypes.c_uint(0)
-    _call("cuda_operator_lab_gemm_status", ctypes.byref(value), ctypes.c_int(1 if clear else 0))
+    _call("cuda_operator_lab_gemm_status", ctypes.byref(value), int(1 if clear else 0))
     return int(value.value)
 
 
 def device_info() -> dict[str, int]:
     """SM count and compute capability of the current device, as the library sees them."""
-    sm, major, minor = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+    sm, major, minor = int(0), int(0), int(0)
     _call("cuda_operator_lab_device_info", ctypes.byref(sm), ctypes.byref(major),
           ctypes.byref(minor))
     return {"sm_count": sm.value, "cc_major": major.value, "cc_minor": minor.value}
