@@ -177,6 +177,27 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(device=t.device).cuda_stream
 
 
+def _all_cuda(*tensors: torch.Tensor) -> bool:
+    for t in tensors:
+        if not t.is_cuda:
+            return False
+    return True
+
+
+def _all_contiguous(*tensors: torch.Tensor) -> bool:
+    for t in tensors:
+        if not t.is_contiguous():
+            return False
+    return True
+
+
+def _any_not_dtype(dtype: torch.dtype, *tensors: torch.Tensor) -> bool:
+    for t in tensors:
+        if t.dtype != dtype:
+            return True
+    return False
+
+
 def _call(symbol: str, *args) -> None:
     library = _LIBRARY if _LIBRARY is not None else _library()
     code = library.functions[symbol](*args)
@@ -494,9 +515,9 @@ def _validate_fused_residual_layernorm_input(x: torch.Tensor, residual: torch.Te
         raise ValueError("weight must be 1-D with length equal to cols")
     if bias.ndim != 1 or bias.shape[0] != x.shape[1]:
         raise ValueError("bias must be 1-D with length equal to cols")
-    if any(t.dtype != torch.float32 for t in (x, residual, weight, bias)):
+    if _any_not_dtype(torch.float32, x, residual, weight, bias):
         raise TypeError("fused residual layernorm currently supports float32 only")
-    if not all(t.is_contiguous() for t in (x, residual, weight, bias)):
+    if not _all_contiguous(x, residual, weight, bias):
         raise ValueError("all fused residual layernorm inputs must be contiguous")
     if x.shape[1] == 0:
         raise ValueError("fused residual layernorm requires cols > 0")
@@ -651,7 +672,7 @@ def _make_gemm_bias_gelu(version: int) -> None:
 
     def into(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
              out: torch.Tensor) -> torch.Tensor:
-        if not all(t.is_cuda for t in (x, weight, bias, out)):
+        if not _all_cuda(x, weight, bias, out):
             raise ValueError("GEMM Bias GELU tensors must be CUDA tensors")
         if x.ndim != 2 or weight.ndim != 2:
             raise ValueError("x and weight must be 2-D")
@@ -662,9 +683,9 @@ def _make_gemm_bias_gelu(version: int) -> None:
         expected_shape = (x.shape[0], weight.shape[0])
         if out.shape != expected_shape:
             raise ValueError(f"output shape must be {expected_shape}")
-        if any(t.dtype != torch.float32 for t in (x, weight, bias, out)):
+        if _any_not_dtype(torch.float32, x, weight, bias, out):
             raise TypeError("GEMM Bias GELU currently supports float32 only")
-        if not all(t.is_contiguous() for t in (x, weight, bias, out)):
+        if not _all_contiguous(x, weight, bias, out):
             raise ValueError("all GEMM Bias GELU tensors must be contiguous")
         m, k = x.shape
         n = weight.shape[0]
@@ -691,7 +712,7 @@ for _v in range(7):
 def gemm_bias_gelu_bf16_into(x_bf16: torch.Tensor, weight_bf16: torch.Tensor, bias: torch.Tensor,
                              out_bf16: torch.Tensor) -> torch.Tensor:
     """bf16 tensor-core gelu_erf(x @ W.T + bias) with fp32 accumulation and bf16 output."""
-    if not all(t.is_cuda for t in (x_bf16, weight_bf16, bias, out_bf16)):
+    if not _all_cuda(x_bf16, weight_bf16, bias, out_bf16):
         raise ValueError("GEMM Bias GELU tensors must be CUDA tensors")
     if x_bf16.ndim != 2 or weight_bf16.ndim != 2:
         raise ValueError("x and weight must be 2-D")
@@ -702,11 +723,11 @@ def gemm_bias_gelu_bf16_into(x_bf16: torch.Tensor, weight_bf16: torch.Tensor, bi
     expected_shape = (x_bf16.shape[0], weight_bf16.shape[0])
     if out_bf16.shape != expected_shape:
         raise ValueError(f"output shape must be {expected_shape}")
-    if any(t.dtype != torch.bfloat16 for t in (x_bf16, weight_bf16, out_bf16)):
+    if _any_not_dtype(torch.bfloat16, x_bf16, weight_bf16, out_bf16):
         raise TypeError("GEMM Bias GELU bf16 expects bfloat16 x, weight and output")
     if bias.dtype != torch.float32:
         raise TypeError("GEMM Bias GELU bf16 expects a float32 bias")
-    if not all(t.is_contiguous() for t in (x_bf16, weight_bf16, bias, out_bf16)):
+    if not _all_contiguous(x_bf16, weight_bf16, bias, out_bf16):
         raise ValueError("all GEMM Bias GELU tensors must be contiguous")
     m, k = x_bf16.shape
     n = weight_bf16.shape[0]
@@ -737,7 +758,7 @@ def gemm_residual_bf16_into(x_bf16: torch.Tensor, weight_bf16: torch.Tensor,
     ``out_bf16`` may be ``residual_bf16`` itself (in-place residual update).
     """
     tensors = (x_bf16, weight_bf16, residual_bf16, out_bf16)
-    if not all(t.is_cuda for t in tensors):
+    if not _all_cuda(*tensors):
         raise ValueError("GEMM residual tensors must be CUDA tensors")
     if x_bf16.ndim != 2 or weight_bf16.ndim != 2:
         raise ValueError("x and weight must be 2-D")
@@ -746,9 +767,9 @@ def gemm_residual_bf16_into(x_bf16: torch.Tensor, weight_bf16: torch.Tensor,
     expected_shape = (x_bf16.shape[0], weight_bf16.shape[0])
     if residual_bf16.shape != expected_shape or out_bf16.shape != expected_shape:
         raise ValueError(f"residual and output shape must be {expected_shape}")
-    if any(t.dtype != torch.bfloat16 for t in tensors):
+    if _any_not_dtype(torch.bfloat16, *tensors):
         raise TypeError("GEMM residual bf16 expects bfloat16 tensors")
-    if not all(t.is_contiguous() for t in tensors):
+    if not _all_contiguous(*tensors):
         raise ValueError("all GEMM residual tensors must be contiguous")
     m, k = x_bf16.shape
     n = weight_bf16.shape[0]
@@ -819,7 +840,7 @@ def gemm_swiglu_rowscale_bf16_into(x_bf16: torch.Tensor, row_scale: torch.Tensor
     RMSNorm -> GEMM+SwiGLU block when the weight was folded by :func:`fold_rmsnorm_weight`
     and row_scale comes from :func:`rmsnorm_rstd_bf16`."""
     tensors = (x_bf16, row_scale, packed_weight_bf16, out_bf16)
-    if not all(t.is_cuda for t in tensors):
+    if not _all_cuda(*tensors):
         raise ValueError("GEMM SwiGLU tensors must be CUDA tensors")
     if x_bf16.ndim != 2 or packed_weight_bf16.ndim != 2:
         raise ValueError("x and packed weight must be 2-D")
@@ -831,9 +852,9 @@ def gemm_swiglu_rowscale_bf16_into(x_bf16: torch.Tensor, row_scale: torch.Tensor
         raise ValueError("row_scale must be a float32 vector of length M")
     if out_bf16.shape != (m, n):
         raise ValueError(f"output shape must be {(m, n)}")
-    if any(t.dtype != torch.bfloat16 for t in (x_bf16, packed_weight_bf16, out_bf16)):
+    if _any_not_dtype(torch.bfloat16, x_bf16, packed_weight_bf16, out_bf16):
         raise TypeError("GEMM SwiGLU row-scale expects bfloat16 x, weight and output")
-    if not all(t.is_contiguous() for t in tensors):
+    if not _all_contiguous(*tensors):
         raise ValueError("all GEMM SwiGLU tensors must be contiguous")
     if m == 0 or n == 0:
         return out_bf16
@@ -869,7 +890,7 @@ def gemm_swiglu_allgather_bf16(x_bf16: torch.Tensor, row_scale: torch.Tensor | N
     :func:`peer_open`.  Enqueued on the current stream of x's device; follow it
     with :func:`peer_barrier` before reading blocks other ranks wrote."""
     tensors = [x_bf16, packed_weight_bf16] + ([row_scale] if row_scale is not None else [])
-    if not all(t.is_cuda for t in tensors):
+    if not _all_cuda(*tensors):
         raise ValueError("GEMM SwiGLU tensors must be CUDA tensors")
     if x_bf16.ndim != 2 or packed_weight_bf16.ndim != 2:
         raise ValueError("x and packed weight must be 2-D")
@@ -877,7 +898,7 @@ def gemm_swiglu_allgather_bf16(x_bf16: torch.Tensor, row_scale: torch.Tensor | N
         raise ValueError("packed weight must be [2N, K] with K = x.shape[1]")
     if x_bf16.dtype != torch.bfloat16 or packed_weight_bf16.dtype != torch.bfloat16:
         raise TypeError("GEMM SwiGLU all-gather expects bfloat16 x and weight")
-    if not all(t.is_contiguous() for t in tensors):
+    if not _all_contiguous(*tensors):
         raise ValueError("all GEMM SwiGLU tensors must be contiguous")
     n = packed_weight_bf16.shape[0] // 2
     m, k = x_bf16.shape
@@ -963,7 +984,7 @@ def _make_gemm_swiglu_f32_dual(version: int) -> None:
 
     def into(x: torch.Tensor, gate_weight: torch.Tensor, up_weight: torch.Tensor,
              workspace: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        if not all(t.is_cuda for t in (x, gate_weight, up_weight, workspace, out)):
+        if not _all_cuda(x, gate_weight, up_weight, workspace, out):
             raise ValueError("GEMM SwiGLU tensors must be CUDA tensors")
         if x.ndim != 2 or gate_weight.ndim != 2 or up_weight.ndim != 2:
             raise ValueError("x and weights must be 2-D")
@@ -974,9 +995,9 @@ def _make_gemm_swiglu_f32_dual(version: int) -> None:
         expected_shape = (x.shape[0], gate_weight.shape[0])
         if workspace.shape != expected_shape or out.shape != expected_shape:
             raise ValueError(f"workspace and output shape must be {expected_shape}")
-        if any(t.dtype != torch.float32 for t in (x, gate_weight, up_weight, workspace, out)):
+        if _any_not_dtype(torch.float32, x, gate_weight, up_weight, workspace, out):
             raise TypeError("GEMM SwiGLU currently supports float32 only")
-        if not all(t.is_contiguous() for t in (x, gate_weight, up_weight, workspace, out)):
+        if not _all_contiguous(x, gate_weight, up_weight, workspace, out):
             raise ValueError("all GEMM SwiGLU tensors must be contiguous")
         m, k = x.shape
         n = gate_weight.shape[0]
@@ -1008,7 +1029,7 @@ def _make_gemm_swiglu_packed(version: int, in_dtype: torch.dtype, ws_dtype: torc
 
     def into(x: torch.Tensor, packed_weight: torch.Tensor, workspace: torch.Tensor,
              out: torch.Tensor) -> torch.Tensor:
-        if not all(t.is_cuda for t in (x, packed_weight, workspace, out)):
+        if not _all_cuda(x, packed_weight, workspace, out):
             raise ValueError(f"GEMM SwiGLU {tag} tensors must be CUDA tensors")
         if x.ndim != 2 or packed_weight.ndim != 2:
             raise ValueError("x_bf16 and packed_weight_bf16 must be 2-D" if bf16
@@ -1041,9 +1062,9 @@ def _make_gemm_swiglu_packed(version: int, in_dtype: torch.dtype, ws_dtype: torc
             raise ValueError(f"workspace shape must be {expected_workspace}")
         if out.shape != expected_out:
             raise ValueError(f"output shape must be {expected_out}")
-        if not bf16 and any(t.dtype != torch.float32 for t in (x, packed_weight, workspace, out)):
+        if not bf16 and _any_not_dtype(torch.float32, x, packed_weight, workspace, out):
             raise TypeError(f"GEMM SwiGLU {tag} currently supports float32 only")
-        if not all(t.is_contiguous() for t in (x, packed_weight, workspace, out)):
+        if not _all_contiguous(x, packed_weight, workspace, out):
             raise ValueError(f"all GEMM SwiGLU {tag} tensors must be contiguous")
         m, k = x.shape
         if m == 0 or n == 0:
@@ -1080,7 +1101,7 @@ def _make_gemm_swiglu_bf16_dual(version: int) -> None:
     def into(x_bf16: torch.Tensor, gate_weight_bf16: torch.Tensor, up_weight_bf16: torch.Tensor,
              out: torch.Tensor) -> torch.Tensor:
         tensors = (x_bf16, gate_weight_bf16, up_weight_bf16, out)
-        if not all(t.is_cuda for t in tensors):
+        if not _all_cuda(*tensors):
             raise ValueError(f"GEMM SwiGLU {tag} tensors must be CUDA tensors")
         if x_bf16.ndim != 2 or gate_weight_bf16.ndim != 2 or up_weight_bf16.ndim != 2:
             raise ValueError("x and weights must be 2-D")
@@ -1088,14 +1109,14 @@ def _make_gemm_swiglu_bf16_dual(version: int) -> None:
             raise ValueError("gate and up weights must have the same shape")
         if x_bf16.shape[1] != gate_weight_bf16.shape[1]:
             raise ValueError("x.shape[1] must equal weight.shape[1]")
-        if any(t.dtype != torch.bfloat16 for t in (x_bf16, gate_weight_bf16, up_weight_bf16)):
+        if _any_not_dtype(torch.bfloat16, x_bf16, gate_weight_bf16, up_weight_bf16):
             raise TypeError(f"GEMM SwiGLU {tag} expects BF16 input and weights")
         if out.dtype != torch.float32:
             raise TypeError(f"GEMM SwiGLU {tag} output must be float32")
         expected_out = (x_bf16.shape[0], gate_weight_bf16.shape[0])
         if out.shape != expected_out:
             raise ValueError(f"output shape must be {expected_out}")
-        if not all(t.is_contiguous() for t in tensors):
+        if not _all_contiguous(*tensors):
             raise ValueError(f"all GEMM SwiGLU {tag} tensors must be contiguous")
         m, k = x_bf16.shape
         n = gate_weight_bf16.shape[0]
@@ -1145,7 +1166,7 @@ def gemm_swiglu_bf16_into(x_bf16: torch.Tensor, packed_weight_bf16: torch.Tensor
     both projections stay in tensor memory until the fused epilogue.
     """
     tensors = (x_bf16, packed_weight_bf16, out_bf16)
-    if not all(t.is_cuda for t in tensors):
+    if not _all_cuda(*tensors):
         raise ValueError("GEMM SwiGLU bf16 tensors must be CUDA tensors")
     if x_bf16.ndim != 2 or packed_weight_bf16.ndim != 2:
         raise ValueError("x_bf16 and packed_weight_bf16 must be 2-D")
@@ -1153,13 +1174,13 @@ def gemm_swiglu_bf16_into(x_bf16: torch.Tensor, packed_weight_bf16: torch.Tensor
         raise ValueError("x_bf16.shape[1] must equal packed_weight_bf16.shape[1]")
     if packed_weight_bf16.shape[0] % 2 != 0:
         raise ValueError("packed_weight_bf16.shape[0] must be even")
-    if any(t.dtype != torch.bfloat16 for t in tensors):
+    if _any_not_dtype(torch.bfloat16, *tensors):
         raise TypeError("GEMM SwiGLU bf16 expects bfloat16 input, packed weight and output")
     n = packed_weight_bf16.shape[0] // 2
     expected_out = (x_bf16.shape[0], n)
     if out_bf16.shape != expected_out:
         raise ValueError(f"output shape must be {expected_out}")
-    if not all(t.is_contiguous() for t in tensors):
+    if not _all_contiguous(*tensors):
         raise ValueError("all GEMM SwiGLU bf16 tensors must be contiguous")
     m, k = x_bf16.shape
     if m == 0 or n == 0:
@@ -1193,7 +1214,7 @@ def gemm_status(clear: bool = True) -> int:
 
 def device_info() -> dict[str, int]:
     """SM count and compute capability of the current device, as the library sees them."""
-    sm, major, minor = int(0), int(0), int(0)
+    sm, major, minor = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
     _call("cuda_operator_lab_device_info", ctypes.byref(sm), ctypes.byref(major),
           ctypes.byref(minor))
     return {"sm_count": sm.value, "cc_major": major.value, "cc_minor": minor.value}

@@ -39,8 +39,11 @@ def _operands(m, k, n, seed):
 @pytest.mark.parametrize("scaled", [False, True])
 @pytest.mark.parametrize(("world", "m", "k", "n"), [
     (2, 512, 1024, 1792), (4, 300, 512, 1024), (8, 256, 2048, 14336 // 8), (8, 130, 256, 1000),
-    (3, 1, 64, 96), (2, 2048, 512, 2 * 112), (2, 640, 512, 2 * 96), (2, 384, 256, 2 * 64)])
+    (3, 1, 64, 96), (2, 2048, 512, 2 * 112), (2, 640, 512, 2 * 96), (2, 384, 256, 2 * 64),
+    (1, 2048, 1024, 1792)])
 def test_gather_epilogue_fills_every_destination(world, m, k, n, scaled):
+    # (1, 2048, 1024, 1792): 112 CTA-pair tiles end in a stream-K tail, in the
+    # gathering kernel and in the plain one alike
     x, packed, rs = _operands(m, k, n, world * 7 + m)
     rs = rs if scaled else None
     if scaled:
@@ -59,6 +62,34 @@ def test_gather_epilogue_fills_every_destination(world, m, k, n, scaled):
     assert b.gemm_status() == 0
     for buf in bufs:
         assert torch.equal(buf, full)
+
+
+def test_gather_at_the_headline_shard_shape_matches_the_oracle():
+    """The 8-rank N split of the benchmark workload (K=4096, N=14336, each rank
+    1792 columns; M=2048 of its 16384 rows), ranks emulated in turn: every
+    destination holds the same blocks, and 256 rows of them match the CPU
+    oracle of the row-scaled GEMM+SwiGLU at the bf16 bar."""
+    from oracle import reference_math as oracle
+
+    world, m, k, n = 8, 2048, 4096, 14336
+    x, packed, rs = _operands(m, k, n, 20261230)
+    bufs = [torch.full((m, n), float("nan"), device=DEV, dtype=torch.bfloat16)
+            for _ in range(world)]
+    b.gemm_status(clear=True)
+    for r in range(world):
+        lo, _ = sharding.shard_range(n, r, world)
+        shard = sharding.pack_gate_up_shard(packed, r, world)
+        dests = [bufs[(r + j) % world].data_ptr() + lo * 2 for j in range(world)]
+        b.gemm_swiglu_allgather_bf16(x, rs, shard, dests, n)
+    torch.cuda.synchronize()
+    assert b.gemm_status() == 0
+    for buf in bufs[1:]:
+        assert torch.equal(buf, bufs[0])
+    rows = torch.arange(0, m, 8) + torch.arange(0, m, 8) % 7
+    expected = oracle.gemm_swiglu_rowscale_bf16(x[rows.to(DEV)].cpu(), rs[rows.to(DEV)].cpu(),
+                                                packed.cpu())
+    torch.testing.assert_close(bufs[0][rows.to(DEV)].cpu().float(), expected.float(),
+                               rtol=2e-2, atol=2e-2)
 
 
 def test_gather_argument_checks():
@@ -164,8 +195,18 @@ def _ranks_worker(rank: int, world: int, port: int, results, layout: str) -> Non
             out = gather(x, shard, scale)
             expected = _as_layout(b.gemm_swiglu_rowscale_bf16(x, scale, packed), world, layout)
             ok = ok and torch.equal(out, expected)
-        ok = ok and torch.equal(gather(x, shard, rs), _as_layout(full, world, layout))
-        del out
+        last = gather(x, shard, rs)
+        ok = ok and torch.equal(last, _as_layout(full, world, layout))
+        # and against the CPU oracle on a row sample, at the bf16 bar
+        from oracle import reference_math as oracle
+
+        rows = torch.arange(0, m, 37)
+        expected = _as_layout(oracle.gemm_swiglu_rowscale_bf16(
+            x[rows.to(x.device)].cpu(), rs[rows.to(x.device)].cpu(), packed.cpu()), world, layout)
+        got = last[:, rows.to(x.device)] if layout == "blocks" else last[rows.to(x.device)]
+        ok = ok and torch.allclose(got.cpu().float(), expected.float(), rtol=2e-2, atol=2e-2)
+        gather.check()
+        del out, last
         results[rank] = (ok, b.peer_status(), b.gemm_status())
     finally:
         if gather is not None:

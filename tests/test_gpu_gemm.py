@@ -99,8 +99,12 @@ def test_dual_bf16_swiglu_shape_guards(version, m, k, n):
         getattr(b, f"gemm_swiglu_v{version}")(x.to(DEV), wg.to(DEV), wu.to(DEV))
 
 
+# (16384, 512, 1792) and (8192, 1024, 1792) end in a nearly empty wave of
+# CTA-pair tiles, which the stream-K tail re-deals as equal shares of k-blocks
+# (a split tile finished with the next pair's partial accumulator)
 @pytest.mark.parametrize(("m", "k", "n"), [(1, 8, 1), (16, 64, 64), (100, 256, 300),
-                                           (128, 64, 2048), (512, 4096, 4096), (1000, 1024, 1500)])
+                                           (128, 64, 2048), (512, 4096, 4096), (1000, 1024, 1500),
+                                           (16384, 512, 1792), (8192, 1024, 1792)])
 def test_gemm_swiglu_bf16_output(m, k, n):
     x, wg, wu = bf16_inputs(m, k, n, 20261201 + m + k + n)
     packed = torch.cat((wg, wu), dim=0).contiguous()
@@ -306,6 +310,16 @@ def test_split_k_gemm_is_bitwise_stable():
     first = b.gemm_bias_gelu_bf16(x, w, bias)
     for _ in range(3):
         assert torch.equal(b.gemm_bias_gelu_bf16(x, w, bias), first)
+
+
+def test_stream_k_tail_is_bitwise_stable():
+    # fixed shares and a fixed order of the two partial sums of a split tile
+    x, wg, wu = bf16_inputs(8192, 1024, 1792, 79)
+    packed = torch.cat((wg, wu), 0).contiguous().to(DEV)
+    xd = x.to(DEV)
+    first = b.gemm_swiglu_bf16(xd, packed)
+    for _ in range(3):
+        assert torch.equal(b.gemm_swiglu_bf16(xd, packed), first)
 
 
 def test_gemm_repeated_calls_are_bitwise_stable():
