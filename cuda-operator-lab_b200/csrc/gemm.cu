@@ -303,15 +303,6 @@ struct GatherOut {
   void* peers[col::sm100::kMaxPeers];
 };
 
-template <int EPI, typename TOut, bool FLUSH>
-int launch_chosen(GemmParams& p, cudaStream_t s, int dev, bool use_pair, int bnh, int pair_slots,
-                  int sm_count);
-
-// Stream-K tail limits: k-blocks per tile worth splitting, and the largest
-// number of waves for which the re-dealt last wave still pays.
-constexpr int kStreamKMinKBlocks = 8;
-constexpr int kStreamKMaxWaves = 48;
-
 template <int EPI, typename TOut, bool FLUSH = false>
 int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, void* out,
                        std::uint64_t m, std::uint64_t n, cudaStream_t s,
@@ -423,51 +414,6 @@ int launch_tensor_gemm(const TcOperands& ops, BMode mode, const float* bias, voi
     }
   }
   p.flush_k_blocks = FLUSH ? kFlushKBlocks : 0;
-  // Stream-K tail for the CTA-pair kernel: when the last wave of tiles would
-  // leave most pairs idle (under 80 % full) and there are few waves, the
-  // last full wave and the partial one are re-dealt as equal shares of
-  // k-blocks (gemm_sm100_2sm.cuh).  Scratch: one fp32 partial accumulator per
-  // pair and one flag per epilogue warp, stream-ordered from the library's
-  // pool, the flags cleared on the stream.
-  void* sk_scratch = nullptr;
-  if constexpr (!FLUSH) {
-    if (use_pair && ops.k_blocks >= kStreamKMinKBlocks) {
-      const int tiles = p.num_m_blocks * p.num_n_blocks;
-      const int pairs = tiles < pair_slots ? tiles : pair_slots;
-      const int rem = pairs > 0 ? tiles % pairs : 0;
-      const int waves = pairs > 0 ? (tiles + pairs - 1) / pairs : 0;
-      if (tiles > pairs && rem != 0 && rem * 10 < pairs * 8 && waves <= kStreamKMaxWaves) {
-        const std::size_t part_bytes = static_cast<std::size_t>(pairs) * 2 * 1024 * bnh;
-        const std::size_t flag_bytes = static_cast<std::size_t>(pairs) * 2 * col::sm100::kEpiWarps * 4;
-        if (col::scratch_alloc(&sk_scratch, part_bytes + flag_bytes, s) == cudaSuccess) {
-          p.sk_dp_tiles = (tiles / pairs - 1) * pairs;
-          p.sk_partials = static_cast<uint8_t*>(sk_scratch);
-          p.sk_flags = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(sk_scratch) + part_bytes);
-          const cudaError_t me = cudaMemsetAsync(p.sk_flags, 0, flag_bytes, s);
-          if (me != cudaSuccess) {
-            cudaFreeAsync(sk_scratch, s);
-            return static_cast<int>(me);
-          }
-        } else {
-          cudaGetLastError();
-          sk_scratch = nullptr;
-        }
-      }
-    }
-  }
-  const int launch_rc = launch_chosen<EPI, TOut, FLUSH>(p, s, dev, use_pair, bnh, pair_slots,
-                                                         info.sm_count);
-  if (sk_scratch != nullptr) {
-    const cudaError_t fe = cudaFreeAsync(sk_scratch, s);
-    if (launch_rc == 0 && fe != cudaSuccess) return static_cast<int>(fe);
-  }
-  return launch_rc;
-}
-
-template <int EPI, typename TOut, bool FLUSH>
-int launch_chosen(GemmParams& p, cudaStream_t s, int dev, bool use_pair, int bnh, int pair_slots,
-                  int sm_count) {
-  int rc = 0;
   if constexpr (FLUSH) {
     if (use_pair) {
       switch (bnh) {
@@ -483,9 +429,9 @@ int launch_chosen(GemmParams& p, cudaStream_t s, int dev, bool use_pair, int bnh
       }
     }
     switch (bnh) {  // choose_bnh offers 128, 96 and 64 only here
-      case 128: return launch_tc<128, EPI, TOut, true>(p, s, dev, sm_count);
-      case 96: return launch_tc<96, EPI, TOut, true>(p, s, dev, sm_count);
-      default: return launch_tc<64, EPI, TOut, true>(p, s, dev, sm_count);
+      case 128: return launch_tc<128, EPI, TOut, true>(p, s, dev, info.sm_count);
+      case 96: return launch_tc<96, EPI, TOut, true>(p, s, dev, info.sm_count);
+      default: return launch_tc<64, EPI, TOut, true>(p, s, dev, info.sm_count);
     }
   } else {
     if (use_pair) {
@@ -506,11 +452,11 @@ int launch_chosen(GemmParams& p, cudaStream_t s, int dev, bool use_pair, int bnh
       }
     }
     switch (bnh) {
-      case 128: return launch_tc<128, EPI, TOut, false>(p, s, dev, sm_count);
-      case 112: return launch_tc<112, EPI, TOut, false>(p, s, dev, sm_count);
-      case 96: return launch_tc<96, EPI, TOut, false>(p, s, dev, sm_count);
-      case 32: return launch_tc<32, EPI, TOut, false>(p, s, dev, sm_count);
-      default: return launch_tc<64, EPI, TOut, false>(p, s, dev, sm_count);
+      case 128: return launch_tc<128, EPI, TOut, false>(p, s, dev, info.sm_count);
+      case 112: return launch_tc<112, EPI, TOut, false>(p, s, dev, info.sm_count);
+      case 96: return launch_tc<96, EPI, TOut, false>(p, s, dev, info.sm_count);
+      case 32: return launch_tc<32, EPI, TOut, false>(p, s, dev, info.sm_count);
+      default: return launch_tc<64, EPI, TOut, false>(p, s, dev, info.sm_count);
     }
   }
 }

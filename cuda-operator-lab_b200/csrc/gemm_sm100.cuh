@@ -101,15 +101,6 @@ struct __align__(64) GemmParams {
   // buffers of other GPUs, mapped into this process (peer stores over NVLink).
   int num_peers;
   void* peer_out[kMaxPeers];
-  // Stream-K tail (CTA-pair kernel, gemm_sm100_2sm.cuh): when sk_flags is not
-  // null, tiles [0, sk_dp_tiles) are dealt whole, round robin, and the k-blocks
-  // of the remaining tiles are split evenly over the CTA pairs; a tile split
-  // between pairs c and c+1 is finished by c with c+1's fp32 partial
-  // accumulator, read from sk_partials (2 * 1024 * BNH bytes per pair) once
-  // the kEpiWarps flags sk_flags[((c + 1) * 2 + rank) * kEpiWarps + w] are set.
-  int sk_dp_tiles;
-  uint8_t* sk_partials;
-  unsigned* sk_flags;
 };
 
 // Column (x) coordinates of k-block kb in A and in B.
@@ -621,35 +612,10 @@ struct GatherSplit {
   __device__ __forceinline__ static int last(int group) { return group == 0 ? kChunks0 : kChunks; }
 };
 
-// Partial-accumulator hooks of the stream-K tail (gemm_sm100_2sm.cuh): the
-// offset of a row's 16-column segment j in one CTA's partial, and the add.
-template <int BNH>
-__device__ __forceinline__ uint32_t partial_offset(int q, int col, int j, int lane) {
-  constexpr int kChunks = 2 * BNH / (16 * kEpiGroups);  // chunks per warp
-  const int group = (col >> 4) % kEpiGroups;
-  const int i = col / (16 * kEpiGroups);
-  const int w = q + 4 * group;
-  return static_cast<uint32_t>((((w * kChunks + i) * 4 + j) * 32 + lane) * 16);
-}
-
-__device__ __forceinline__ void add_partial16(const uint8_t* part, uint32_t off0, float (&v)[16]) {
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float4 f = *reinterpret_cast<const float4*>(part + off0 + j * 32 * 16);
-    v[4 * j + 0] += f.x;
-    v[4 * j + 1] += f.y;
-    v[4 * j + 2] += f.z;
-    v[4 * j + 3] += f.w;
-  }
-}
-
-// `part`: the partner pair's partial accumulator to add first (stream-K), or
-// null; q = this warp's TMEM lane quarter.
 template <int BNH>
 __device__ __forceinline__ void epilogue_gather_local(const GemmParams& p, int row, int nb,
                                                       uint32_t t_row, int group, int lane,
-                                                      uint8_t* stage, int q = 0,
-                                                      const uint8_t* part = nullptr) {
+                                                      uint8_t* stage) {
   using Split = GatherSplit<BNH>;
   const int c0 = Split::first(group);
   const int c1 = Split::last(group);
@@ -662,21 +628,11 @@ __device__ __forceinline__ void epilogue_gather_local(const GemmParams& p, int r
     const int c = ci * 16;
     uint32_t g[16], u[16];
     tmem_ld16x2(t_row + c, t_row + BNH + c, g, u);
-    float gv[16], uv[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      gv[j] = __uint_as_float(g[j]);
-      uv[j] = __uint_as_float(u[j]);
-    }
-    if (part != nullptr) {
-      add_partial16(part, partial_offset<BNH>(q, c, 0, lane), gv);
-      add_partial16(part, partial_offset<BNH>(q, BNH + c, 0, lane), uv);
-    }
     float o[16], lo[8], hi[8];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       // rs = 1 multiplies exactly: the same bits as the unscaled epilogue
-      o[j] = silu_fast(gv[j] * rs) * (uv[j] * rs);
+      o[j] = silu_fast(__uint_as_float(g[j]) * rs) * (__uint_as_float(u[j]) * rs);
     }
     store_chunk<__nv_bfloat16, 16>(p, row, col_base + c, o);
 #pragma unroll

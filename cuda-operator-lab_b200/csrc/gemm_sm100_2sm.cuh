@@ -131,199 +131,6 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols)
                : "memory");
 }
 
-// ------------------------------------------------------------ stream-K tail
-//
-// Work of one CTA pair: whole tiles c, c + P, ... below p.sk_dp_tiles (all
-// tiles when stream-K is off), then -- stream-K on -- an even share of the
-// k-blocks of the remaining tiles, taken in tile order.  Every share is at
-// least one tile long, so a tile is split at most once, between pairs c and
-// c+1: pair c+1 computes the tile's last k-blocks first thing in its share
-// (kind kWorkTail: the accumulator goes to global memory and a flag is set),
-// pair c its first k-blocks last (kind kWorkHead: it adds c+1's partial and
-// runs the epilogue).  All three roles walk the same sequence.
-constexpr int kWorkFull = 0;
-constexpr int kWorkTail = 1;
-constexpr int kWorkHead = 2;
-
-struct WorkItem {
-  int tile;
-  int kb0;
-  int kb1;
-  int kind;
-};
-
-struct WorkSched {
-  int pair, pairs, dp_end, next_dp, kbs;
-  uint64_t u, u_end;
-  bool sk;
-
-  __device__ __forceinline__ WorkSched(const GemmParams& p, int c, int num_pairs)
-      : pair(c), pairs(num_pairs), next_dp(c), kbs(p.num_k_blocks), u(0), u_end(0) {
-    const int num_tiles = p.num_m_blocks * p.num_n_blocks;
-    sk = p.sk_flags != nullptr;
-    dp_end = sk ? p.sk_dp_tiles : num_tiles;
-    if (sk) {
-      const uint64_t units = static_cast<uint64_t>(num_tiles - dp_end) * static_cast<uint64_t>(kbs);
-      u = units * static_cast<uint64_t>(c) / static_cast<uint64_t>(num_pairs);
-      u_end = units * static_cast<uint64_t>(c + 1) / static_cast<uint64_t>(num_pairs);
-    }
-  }
-
-  __device__ __forceinline__ bool next(WorkItem& w) {
-    if (next_dp < dp_end) {
-      w.tile = next_dp;
-      w.kb0 = 0;
-      w.kb1 = kbs;
-      w.kind = kWorkFull;
-      next_dp += pairs;
-      return true;
-    }
-    if (u < u_end) {
-      const uint64_t t = u / static_cast<uint64_t>(kbs);
-      w.tile = dp_end + static_cast<int>(t);
-      w.kb0 = static_cast<int>(u - t * static_cast<uint64_t>(kbs));
-      const uint64_t left = u_end - u;
-      w.kb1 = static_cast<int>(min(static_cast<uint64_t>(kbs), static_cast<uint64_t>(w.kb0) + left));
-      w.kind = w.kb0 > 0 ? kWorkTail : (w.kb1 < kbs ? kWorkHead : kWorkFull);
-      u += static_cast<uint64_t>(w.kb1 - w.kb0);
-      return true;
-    }
-    return false;
-  }
-};
-
-// One CTA's partial accumulator (128 rows x 2*BNH fp32) is laid out as the
-// epilogue deals its columns (16-column chunks round robin over the
-// kEpiGroups warps of a lane quarter; partial_offset in gemm_sm100.cuh), so
-// each warp writes -- and reads back -- 512 contiguous bytes per (chunk,
-// segment).
-template <int BNH>
-constexpr uint32_t partial_cta_bytes() {
-  return static_cast<uint32_t>(128 * 2 * BNH * 4);
-}
-
-// kWorkTail: this thread's accumulator row, every column, to global memory.
-template <int BNH>
-__device__ __forceinline__ void epilogue_dump_partial(uint32_t t_row, int q, int group, int lane,
-                                                      uint8_t* part) {
-#pragma unroll 1
-  for (int c = group * 16; c < 2 * BNH; c += 16 * kEpiGroups) {
-    uint32_t a[16];
-    tmem_ld16(t_row + c, a);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      *reinterpret_cast<uint4*>(part + partial_offset<BNH>(q, c, j, lane)) =
-          make_uint4(a[4 * j], a[4 * j + 1], a[4 * j + 2], a[4 * j + 3]);
-    }
-  }
-}
-
-// kWorkHead: the epilogue of epilogue_tile with the partner's partial (in
-// shared memory, partial_offset layout) added to the accumulator first.
-template <int BNH, int EPI, typename TOut>
-__device__ __forceinline__ void epilogue_tile_with_partial(const GemmParams& p, int row, int nb,
-                                                           uint32_t t_row, int q, int group,
-                                                           int lane, const uint8_t* part) {
-  if constexpr (EPI == kEpiSwiGLU || EPI == kEpiSwiGLURoundBf16 || EPI == kEpiSwiGLURowScale) {
-    const int col_base = nb * BNH;
-    float rs = 1.0f;
-    if constexpr (EPI == kEpiSwiGLURowScale) rs = row < p.m ? __ldg(p.row_scale + row) : 0.0f;
-#pragma unroll 1
-    for (int c = group * 16; c < BNH; c += 16 * kEpiGroups) {
-      uint32_t g[16], u[16];
-      tmem_ld16x2(t_row + c, t_row + BNH + c, g, u);
-      float gv[16], uv[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        gv[j] = __uint_as_float(g[j]);
-        uv[j] = __uint_as_float(u[j]);
-      }
-      add_partial16(part, partial_offset<BNH>(q, c, 0, lane), gv);
-      add_partial16(part, partial_offset<BNH>(q, BNH + c, 0, lane), uv);
-      float o[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float a = gv[j], b = uv[j];
-        if constexpr (EPI == kEpiSwiGLURoundBf16) {
-          a = bf16_round(a);
-          b = bf16_round(b);
-        } else if constexpr (EPI == kEpiSwiGLURowScale) {
-          a *= rs;
-          b *= rs;
-        }
-        o[j] = silu_fast(a) * b;
-      }
-      store_chunk<TOut, 16>(p, row, col_base + c, o);
-    }
-  } else {
-    const int col_base = nb * 2 * BNH;
-#pragma unroll 1
-    for (int c = group * 16; c < 2 * BNH; c += 16 * kEpiGroups) {
-      uint32_t a[16];
-      tmem_ld16(t_row + c, a);
-      float v[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(a[j]);
-      add_partial16(part, partial_offset<BNH>(q, c, 0, lane), v);
-      float o[16];
-      if constexpr (EPI == kEpiResidual) {
-        float res[16];
-        load_residual16(p, row, col_base + c, res);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) o[j] = v[j] + res[j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int colj = col_base + c + j;
-          const float z = v[j] + (colj < p.n ? __ldg(p.bias + colj) : 0.0f);
-          if constexpr (EPI == kEpiBiasGeluErf) {
-            o[j] = gelu_erf_f(z);
-          } else {
-            o[j] = gelu_tanh_f(z);
-          }
-        }
-      }
-      store_chunk<TOut, 16>(p, row, col_base + c, o);
-    }
-  }
-}
-
-__device__ __forceinline__ void st_release_gpu(unsigned* addr, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* addr) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-  return v;
-}
-
-// Bounded wait for a flag that another CTA pair sets.
-__device__ __forceinline__ bool wait_flag(const unsigned* flag, volatile int* abort_flag) {
-  uint64_t t0 = 0;
-  for (uint32_t i = 1;; ++i) {
-    if (ld_acquire_gpu(flag) != 0u) return true;
-    __nanosleep(128);
-    if ((i & 15u) == 0u) {
-      if (*abort_flag) return false;
-      const uint64_t now = globaltimer_ns();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > kWaitLimitNs) {
-        return false;
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ void bulk_load_global(uint32_t dst, const void* src, uint32_t bytes,
-                                                 uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
-      : "memory");
-}
-
 // Pair tiles: p.num_m_blocks counts 256-row pair blocks here.
 template <int BNH, int EPI, typename TOut, bool FLUSH = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
@@ -333,10 +140,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
   static_assert(EPI != kEpiSwiGLUGather || (sizeof(TOut) == 2 && !FLUSH), "gather: bf16 out");
   constexpr int kStages = Cfg::kStages;
   constexpr uint32_t kIdesc = idesc_bf16_f32(Cfg::kMmaM, Cfg::kMmaN);
-  // stream-K is never set up for the fp32 emulation
-  constexpr bool kStreamK = !FLUSH;
-  static_assert(!kStreamK || Cfg::kStages * Cfg::kStageBytes >= partial_cta_bytes<BNH>(),
-                "a partial accumulator must fit in the operand ring");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -347,10 +150,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
   uint64_t* tfull_bar = bars + 2 * kStages;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
-  uint64_t* part_bar = drain_bar + 1;  // the partner's partial landed (stream-K)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(part_bar + 1);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  static_assert((2 * kStages + 6) * 8 + 8 <= Cfg::kBarrierBytes, "barrier space");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -358,6 +159,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
   const bool leader = rank == 0;
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
+  const int num_tiles = p.num_m_blocks * p.num_n_blocks;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -369,7 +171,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
       mbar_init(smem_u32(tempty_bar + a), 2 * kEpiWarps);
     }
     mbar_init(smem_u32(drain_bar), 1);
-    mbar_init(smem_u32(part_bar), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     grid_dependents_launch();
@@ -400,16 +201,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
         uint32_t issued_phase = 0;
         int filled = 0;  // loads issued so far, counted up to kStages
         bool ok = true;
-        WorkSched sched(p, cluster_id, num_clusters);
-        WorkItem w;
-        while (ok && sched.next(w)) {
+        for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
           int mb, nb;
-          tile_coords(w.tile, p, mb, nb);
+          tile_coords(tile, p, mb, nb);
           const int a_row = mb * Cfg::kMmaM + static_cast<int>(rank) * kBlockM;
           // SwiGLU: both CTAs use row nb*BNH (of the gate map / the up map);
           // GELU: CTA r loads rows nb*2*BNH + r*BNH of W.
           const int b_row = nb * p.b_row_stride + static_cast<int>(rank) * p.b1_row_offset;
-          for (int kb = w.kb0; kb < w.kb1; kb += kKps) {
+          for (int kb = 0; kb < p.num_k_blocks; kb += kKps) {
             // The first pass over the ring needs no wait (every slot starts
             // empty), and skipping it saves the first wait on a barrier just
             // initialised (~0.4 us measured), which a one-k-block tile feels.
@@ -419,7 +218,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
               ok = false;
               break;
             }
-            const int nk = min(kKps, w.kb1 - kb);
+            const int nk = min(kKps, p.num_k_blocks - kb);
             const uint32_t fb_local = smem_u32(full_bar + stage);
             if (leader) mbar_arrive_expect_tx(fb_local, 2 * nk * Cfg::kKBlockBytes);
             const uint32_t fb = map_to_cta(fb_local, 0);
@@ -466,9 +265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
         bool ok = true;
         bool issued_any = false;
         const int chunks = tile_chunks<FLUSH>(p);
-        WorkSched sched(p, cluster_id, num_clusters);
-        WorkItem w;
-        while (ok && sched.next(w)) {
+        for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
           for (int c = 0; c < chunks; ++c, ++local) {
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
@@ -480,12 +277,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
             tc_fence_after();
             const uint32_t d_tmem = tmem_base + acc * Cfg::kAccStride;
             int kb0, kb1;
-            if constexpr (FLUSH) {
-              chunk_range<FLUSH>(p, c, kb0, kb1);
-            } else {
-              kb0 = w.kb0;
-              kb1 = w.kb1;
-            }
+            chunk_range<FLUSH>(p, c, kb0, kb1);
             for (int kb = kb0; kb < kb1; kb += kKps) {
               if (!mbar_wait(smem_u32(full_bar + stage), phase, abort_flag)) {
                 fail(kStatusMma);
@@ -534,11 +326,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
     (void)gather_stage;
     int local = 0;
     bool ok = true;
-    WorkSched sched(p, cluster_id, num_clusters);
-    WorkItem w;
-    while (ok && sched.next(w)) {
+    for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
       int mb, nb;
-      tile_coords(w.tile, p, mb, nb);
+      tile_coords(tile, p, mb, nb);
       const int row = mb * Cfg::kMmaM + static_cast<int>(rank) * kBlockM + q * 32 + lane;
       ChunkSums<BNH, EPI> sums;
       for (int c = 0; c < chunks; ++c, ++local) {
@@ -553,59 +343,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * Cfg::kAccStride;
         if constexpr (FLUSH) {
           accumulate_chunk<BNH, EPI>(t_row, group, c == 0, sums);
+        } else if constexpr (EPI == kEpiSwiGLUGather) {
+          epilogue_gather_local<BNH>(p, row, nb, t_row, group, lane, gather_stage);
         } else {
-          if (w.kind == kWorkFull) {
-            if constexpr (EPI == kEpiSwiGLUGather) {
-              epilogue_gather_local<BNH>(p, row, nb, t_row, group, lane, gather_stage);
-            } else {
-              epilogue_tile<BNH, EPI, TOut>(p, row, nb, t_row, group);
-            }
-          } else if (w.kind == kWorkTail) {
-            // the tile's last k-blocks: the accumulator goes to this pair's
-            // partial buffer; the flag says it is complete
-            uint8_t* part = p.sk_partials +
-                            (static_cast<std::size_t>(cluster_id) * 2 + rank) * partial_cta_bytes<BNH>();
-            epilogue_dump_partial<BNH>(t_row, q, group, lane, part);
-            // every lane's stores are visible GPU-wide before its warp's flag
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) {
-              st_release_gpu(p.sk_flags + (cluster_id * 2 + rank) * kEpiWarps + (warp - 4), 1u);
-            }
-          } else {
-            // the tile's first k-blocks, the pair's last item: every MMA of
-            // this pair is complete, so the operand ring is free to receive
-            // the next pair's partial (same tile, its last k-blocks)
-            bool got = true;
-            if (warp == 4 && lane == 0) {
-              // every warp of the partner CTA has written its part
-              const unsigned* flags = p.sk_flags + ((cluster_id + 1) * 2 + rank) * kEpiWarps;
-              for (int f = 0; got && f < kEpiWarps; ++f) got = wait_flag(flags + f, abort_flag);
-              if (got) {
-                asm volatile("fence.proxy.async.global;" ::: "memory");
-                const uint8_t* src = p.sk_partials + (static_cast<std::size_t>(cluster_id + 1) * 2 + rank) *
-                                                         partial_cta_bytes<BNH>();
-                mbar_arrive_expect_tx(smem_u32(part_bar), partial_cta_bytes<BNH>());
-                bulk_load_global(smem_u32(smem), src, partial_cta_bytes<BNH>(), smem_u32(part_bar));
-              } else {
-                fail(kStatusEpilogue);
-              }
-            }
-            got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
-            if (got && !epi_wait(smem_u32(part_bar), 0, abort_flag, lane)) {
-              if (lane == 0) fail(kStatusEpilogue);
-              got = false;
-            }
-            if (got) {
-              if constexpr (EPI == kEpiSwiGLUGather) {
-                epilogue_gather_local<BNH>(p, row, nb, t_row, group, lane, gather_stage, q, smem);
-              } else {
-                epilogue_tile_with_partial<BNH, EPI, TOut>(p, row, nb, t_row, q, group, lane, smem);
-              }
-            } else {
-              ok = false;
-            }
-          }
+          epilogue_tile<BNH, EPI, TOut>(p, row, nb, t_row, group);
         }
         tc_fence_before();
         __syncwarp();
@@ -616,11 +357,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kCtaThreads, 1)
       }
       if constexpr (EPI == kEpiSwiGLUGather) {
         // the accumulator is already released: the next tile's MMAs run
-        // while this tile travels to the peers (a stream-K tail part has no
-        // output of its own)
-        if (ok && w.kind != kWorkTail) {
-          epilogue_gather_peers<BNH>(p, row - lane, nb, group, lane, gather_stage);
-        }
+        // while this tile travels to the peers
+        if (ok) epilogue_gather_peers<BNH>(p, row - lane, nb, group, lane, gather_stage);
         __syncwarp();
       }
     }

@@ -134,12 +134,7 @@ int cuda_operator_gemm_bias_gelu_v6(const float* input, const float* weight, con
  * Packed versions take W[2N, K] with the N gate rows first, then the N up
  * rows.  The workspace argument is validated (non-NULL) and left untouched:
  * the sm_100a kernel keeps both projections in tensor memory, so there is no
- * [M, 2N] round trip.  Replaces gemm_swiglu.cuh:5-136.
- * Every bf16 tensor-core GEMM of this header may take stream-ordered scratch
- * from the library's memory pool for the call's duration: when its last wave
- * of tiles would leave most SMs idle, that wave is re-dealt stream-K style and
- * a split tile's fp32 partial accumulator passes through the scratch (freed on
- * the stream after the launch; graph memory nodes under capture). */
+ * [M, 2N] round trip.  Replaces gemm_swiglu.cuh:5-136. */
 int cuda_operator_gemm_swiglu_v0(const float* input, const float* gate_weight, const float* up_weight, float* workspace, float* output, uint64_t m, uint64_t k, uint64_t n, void* stream); /* gemm_swiglu.cuh:5   */
 int cuda_operator_gemm_swiglu_v1(const float* input, const float* gate_weight, const float* up_weight, float* workspace, float* output, uint64_t m, uint64_t k, uint64_t n, void* stream); /* gemm_swiglu.cuh:17  */
 int cuda_operator_gemm_swiglu_v2(const float* input, const float* packed_weight, float* workspace, float* output, uint64_t m, uint64_t k, uint64_t n, void* stream); /* gemm_swiglu.cuh:29  */

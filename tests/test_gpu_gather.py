@@ -42,8 +42,7 @@ def _operands(m, k, n, seed):
     (3, 1, 64, 96), (2, 2048, 512, 2 * 112), (2, 640, 512, 2 * 96), (2, 384, 256, 2 * 64),
     (1, 2048, 1024, 1792)])
 def test_gather_epilogue_fills_every_destination(world, m, k, n, scaled):
-    # (1, 2048, 1024, 1792): 112 CTA-pair tiles end in a stream-K tail, in the
-    # gathering kernel and in the plain one alike
+    # (1, 2048, 1024, 1792): 112 CTA-pair tiles, more than one per pair
     x, packed, rs = _operands(m, k, n, world * 7 + m)
     rs = rs if scaled else None
     if scaled:

@@ -99,9 +99,8 @@ def test_dual_bf16_swiglu_shape_guards(version, m, k, n):
         getattr(b, f"gemm_swiglu_v{version}")(x.to(DEV), wg.to(DEV), wu.to(DEV))
 
 
-# (16384, 512, 1792) and (8192, 1024, 1792) end in a nearly empty wave of
-# CTA-pair tiles, which the stream-K tail re-deals as equal shares of k-blocks
-# (a split tile finished with the next pair's partial accumulator)
+# (16384, 512, 1792) and (8192, 1024, 1792): many tiles per CTA pair, ending in a
+# nearly empty last wave (the 8-GPU shard shape of the benchmark, shorter K)
 @pytest.mark.parametrize(("m", "k", "n"), [(1, 8, 1), (16, 64, 64), (100, 256, 300),
                                            (128, 64, 2048), (512, 4096, 4096), (1000, 1024, 1500),
                                            (16384, 512, 1792), (8192, 1024, 1792)])
@@ -312,8 +311,8 @@ def test_split_k_gemm_is_bitwise_stable():
         assert torch.equal(b.gemm_bias_gelu_bf16(x, w, bias), first)
 
 
-def test_stream_k_tail_is_bitwise_stable():
-    # fixed shares and a fixed order of the two partial sums of a split tile
+def test_many_tiles_per_pair_is_bitwise_stable():
+    # several tiles per CTA pair, both TMEM accumulators in turn
     x, wg, wu = bf16_inputs(8192, 1024, 1792, 79)
     packed = torch.cat((wg, wu), 0).contiguous().to(DEV)
     xd = x.to(DEV)
