@@ -96,12 +96,22 @@ class Dist:
 
             # NCCL's communicator set-up lines (ranks, devices, transports) on
             # stderr, so a run's log shows the communicator each rank joined
-            os.environ.setdefault("NCCL_DEBUG", "INFO")
-            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+            # (an environment asking for the version line only gets the INIT
+            # lines as well)
+            if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+                os.environ["NCCL_DEBUG"] = "INFO"
+                os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
             torch.cuda.set_device(self.local_rank)
             dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                     device_id=torch.device("cuda", self.local_rank))
             self.dist = dist
+            # one collective, so the communicator exists (NCCL creates it lazily)
+            # and its set-up lines precede the run; then a summary of this rank
+            t = torch.ones(1, device="cuda")
+            dist.all_reduce(t)
+            print(f"[bench] rank {self.rank}/{self.world}: NCCL communicator of "
+                  f"{int(t.item())} ranks on cuda:{self.local_rank} "
+                  f"({torch.cuda.get_device_name(self.local_rank)})", file=sys.stderr, flush=True)
         elif torch.cuda.is_available():
             torch.cuda.set_device(0)
 
