@@ -99,8 +99,9 @@ _RESTYPES = {
 #: The 54 symbols of the reference library (``bindings.py:32-417``).
 REFERENCE_SYMBOLS = tuple(
     name for name in _SIGNATURES
-    if name.startswith("cuda_operator_") and not name.startswith("cuda_operator_lab_")
-    and not name.endswith(("_bf16", "_h", "_partial_f64"))
+    if name == "cuda_operator_error_string"
+    or (name.startswith("cuda_operator_") and name.rsplit("_", 1)[-1][:1] == "v"
+        and name.rsplit("_", 1)[-1][1:].isdigit())
 )
 
 
