@@ -6,8 +6,11 @@ GEMM+SwiGLU (M=16384, K=4096, N=14336, W[28672, 4096]) -- as GEMM+SwiGLU
 TFLOP/s for the whole job.  One step = the block as the reference defines it:
 the bf16 RMSNorm of all rows (each rank needs the whole normalised X for its N
 slice) writing the normalised X, then the N-sharded GEMM+SwiGLU with bf16
-output.  Consecutive steps are pipelined over two normalised-X buffers: step
-i's RMSNorm runs on a second stream and overlaps step i-1's GEMM.  All inputs
+output.  With N > 1 ranks the RMSNorm is sharded by rows: each rank
+normalises M/N rows and the copy engines copy them into every rank's X buffer
+over NVLink.  Consecutive steps are pipelined over two normalised-X buffers:
+step i's RMSNorm (and exchange) runs on a second stream and overlaps step
+i-1's GEMM.  All inputs
 are resident in HBM (X 134 MB and W 235 MB exceed the 126 MB L2, so no flush
 between steps is needed).  Scaling is strong: the total work is fixed and rank
 r of N owns output columns [r*N/g, (r+1)*N/g).  Inputs are generated on the
@@ -15,14 +18,17 @@ host from one seed, so the GPU step, the CPU baseline and ``--impl
 reference`` see the same tensors.
 
 Extra keys: ``e2e`` (the same metric through the public API with the X copy
-from pinned host memory and the output shard copied back inside every step,
-uploads, compute and downloads of consecutive steps overlapped on three
-streams; ``serial_value`` without the overlap), ``roofline`` (the GEMM kernel
+from pinned host memory -- at N > 1 each rank its own rows -- and the output
+shard copied back inside every step, uploads, compute and downloads of
+consecutive steps overlapped on three streams; ``serial_value`` without the
+overlap), ``sharded_rmsnorm`` (N > 1: the exchanged normalised X checked
+equal to the unsharded RMSNorm), ``roofline`` (the GEMM kernel
 against the measured bf16 peak: burst for a timed region under a second),
 ``cpu_baseline`` (the CPU oracle, rank 0 at N=1) and ``parity`` (the GPU
 output of the last timed step against that CPU result, every row the CPU
-computed, at the bf16 bar), ``variants`` (the step unpipelined, and with the
-RMSNorm folded into the GEMM), ``clocks`` (nvidia-smi sampled during the
+computed, at the bf16 bar), ``variants`` (the step unpipelined, with the
+RMSNorm folded into the GEMM, and at N > 1 with every rank normalising all
+rows), ``clocks`` (nvidia-smi sampled during the
 timed region), ``gpu_launches`` and ``ops`` (every other BASELINE config:
 per-op device time, GB/s or TFLOP/s and the fraction of the measured peak,
 timed from CUDA graphs of back-to-back calls -- cold rotates over input sets
@@ -91,6 +97,7 @@ class Dist:
         self.rank = int(os.environ.get("RANK", "0"))
         self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
         self.enabled = self.world > 1
+        self.last_region_ms: list[float] = []
         if self.enabled:
             import torch.distributed as dist
 
@@ -127,6 +134,15 @@ class Dist:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
+    def values(self, value: float) -> list[float]:
+        """`value` of every rank, in rank order (one all-gather)."""
+        if not self.enabled:
+            return [value]
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        out = torch.empty(self.world, dtype=torch.float64, device="cuda")
+        self.dist.all_gather_into_tensor(out, t)
+        return [float(v) for v in out.tolist()]
+
     def close(self) -> None:
         if self.enabled:
             self.dist.barrier()
@@ -143,18 +159,26 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpus: list[int]) -> None:
+    def __init__(self, gpus: list[int], enabled: bool = True) -> None:
+        """gpus: nvidia-smi indices of the job's GPUs; one process (rank 0)
+        samples them all, the other ranks pass enabled=False."""
         self.gpus = gpus
+        self.enabled = enabled
         self.proc = None
         self.file = None
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "50"], stdout=self.file, stderr=subprocess.DEVNULL)
-            time.sleep(0.15)
+            # start timing only once nvidia-smi is producing samples
+            deadline = time.time() + 5.0
+            while time.time() < deadline and os.path.getsize(self.file.name) == 0:
+                time.sleep(0.02)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -206,6 +230,16 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- inputs
+
+
+def physical_gpus(world: int) -> list[int]:
+    """nvidia-smi indices of the job's GPUs (CUDA_VISIBLE_DEVICES order when
+    it lists integers, else 0..world-1)."""
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    parts = [v.strip() for v in visible.split(",") if v.strip()]
+    if parts and all(v.isdigit() for v in parts):
+        return [int(v) for v in parts[:world]]
+    return list(range(world))
 
 
 def make_inputs(world: int, rank: int, device: torch.device | str) -> dict:
@@ -261,7 +295,8 @@ def time_region(d: Dist, fn, steps: int, warmup: int, drain=None, after_start=No
     end.synchronize()
     ms = start.elapsed_time(end)
     d.barrier()
-    return d.max(ms)
+    d.last_region_ms = d.values(ms)
+    return max(d.last_region_ms)
 
 
 def event_median_us(fn, reps: int, flush=None) -> float:
@@ -534,61 +569,51 @@ def run_ours(args, d: Dist) -> dict | None:
 
     # One step = the block as the reference defines it: bf16 RMSNorm of every
     # row of X (each rank needs all rows for its N slice) writing normalised X,
-    # then the packed GEMM+SwiGLU of this rank's N slice.  Steps are pipelined
-    # over two normalised-X buffers: step i's RMSNorm runs on a second stream
-    # as soon as the GEMM two steps back has read its buffer, so it overlaps
-    # the previous GEMM's last, partly idle wave of tiles; step i's GEMM waits
-    # for it.  Every step's RMSNorm and GEMM run inside the timed region.
-    # The GEMM's stream has the higher priority: when both kernels are ready,
-    # the block scheduler places the GEMM's CTAs first, and the RMSNorm's take
-    # the SMs that the GEMM's last wave leaves idle (without priorities the
-    # RMSNorm could take SMs at the GEMM's start and delay its persistent CTAs).
-    # CUDA events around every GEMM launch of the timed steps (on the
-    # launching stream) give the dominant kernel's average duration.
-    main = torch.cuda.Stream(priority=-1)
-    main.wait_stream(torch.cuda.current_stream())
-    side = torch.cuda.Stream()
-    xns = [torch.empty_like(x) for _ in range(2)]
-    normed = [torch.cuda.Event() for _ in range(2)]
-    consumed = [torch.cuda.Event() for _ in range(2)]
-    gemm_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                   for _ in range(args.steps)]
-    step_index = [0]
-
-    def step():
-        j = step_index[0] % 2
-        side.wait_event(consumed[j])  # the GEMM two steps back has read xns[j]
-        with torch.cuda.stream(side):
-            b.rmsnorm_bf16_into(x, w_norm, xns[j], EPS)
-            normed[j].record(side)
-        main.wait_event(normed[j])
-        i = step_index[0] - args.warmup
-        if 0 <= i < args.steps:
-            gemm_events[i][0].record(main)
-        b.gemm_swiglu_bf16_into(xns[j], packed, out)
-        if 0 <= i < args.steps:
-            gemm_events[i][1].record(main)
-        consumed[j].record(main)
-        step_index[0] += 1
-
-    def drain():
-        main.wait_stream(side)
-
-    def start(ev):
-        side.wait_event(ev)
-
+    # then the packed GEMM+SwiGLU of this rank's N slice.  With N ranks the
+    # RMSNorm is sharded by rows: each rank normalises its M/N rows and the
+    # copy engines push them into every peer's buffer over NVLink
+    # (sharding.RowNormGather), so no rank repeats the others' work and no SM
+    # is spent on the exchange.  Steps are pipelined over two normalised-X
+    # buffers: step i's RMSNorm (and exchange) runs on a second stream as soon
+    # as the GEMM two steps back has read its buffer -- on every rank, by the
+    # exchange's first barrier -- so it overlaps the previous GEMM; step i's
+    # GEMM waits for it.  Every step's RMSNorm and GEMM run inside the timed
+    # region.  The GEMM's stream has the higher priority: when both kernels
+    # are ready, the block scheduler places the GEMM's CTAs first, and the
+    # RMSNorm's take the SMs that the GEMM's last wave leaves idle.  CUDA
+    # events around every GEMM launch of the timed steps (on the launching
+    # stream) give the dominant kernel's average duration.
     b.gemm_status(clear=True)
-    gpus = list(range(d.world))
-    with ClockSampler(gpus) as clocks, torch.cuda.stream(main):
-        ms = time_region(d, step, args.steps, args.warmup, drain=drain, after_start=start)
-    torch.cuda.current_stream().wait_stream(main)
-    gemm_us = d.max(1000.0 * sum(s_.elapsed_time(e_) for s_, e_ in gemm_events) / args.steps)
+    rng = None
+    if d.world > 1:
+        from cuda_operator_lab import sharding
+
+        rng = sharding.RowNormGather(M, K)
+    try:
+        with ClockSampler(physical_gpus(d.world), enabled=d.rank == 0) as clocks:
+            ms, gemm_rank_us = pipelined_block(d, args, x, w_norm, packed, out, rng)
+        step_ms_ranks = [v / args.steps for v in d.last_region_ms]
+        sharded_norm = None
+        if rng is not None:
+            rng.check()  # raises if an exchange barrier gave up waiting
+            last = rng.outputs[(args.warmup + args.steps - 1) % 2]
+            same = torch.equal(last, b.rmsnorm_bf16(x, w_norm, EPS))
+            sharded_norm = {
+                "identical_to_unsharded": d.max(0.0 if same else 1.0) == 0.0,
+                "rows_per_rank": M // d.world,
+                "nvlink_bytes_per_rank": (d.world - 1) * (M // d.world) * K * 2,
+                "exchange": "cudaMemcpyAsync per peer into its CUDA IPC buffer (copy "
+                            "engines), two device flag barriers per step"}
+    finally:
+        if rng is not None:
+            rng.close()
+    gemm_us_ranks = d.values(gemm_rank_us)
+    gemm_us = max(gemm_us_ranks)
     clock_info = clocks.summary() if d.rank == 0 else None
     status = b.gemm_status(clear=True)
     if status != 0:
         raise RuntimeError(f"GEMM bounded wait timed out (status {status})")
     gpu_out = out.cpu() if d.rank == 0 and d.world == 1 and not args.skip_cpu else None
-    del xns
 
     variants = step_variants(d, args, x, w_norm, packed, out)
 
@@ -635,16 +660,20 @@ def run_ours(args, d: Dist) -> dict | None:
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 4),
+        **({"ms_per_step_ranks": [round(v, 4) for v in step_ms_ranks]} if d.world > 1 else {}),
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) X, N(0,1/K) W, U(0.5,1.5) norm weight)",
         "config": {"workload": "llama_mlp_block (BASELINE config 5)", "M": M, "K": K, "N": N,
-                   "rmsnorm": "bf16 RMSNorm of all 16384 rows on every rank (writes the "
-                              "normalised X the GEMM reads: the reference's block semantics); "
-                              "step i's RMSNorm on a second stream into one of two X buffers, "
-                              "overlapping step i-1's GEMM",
+                   "rmsnorm": ("bf16 RMSNorm of all 16384 rows writing the normalised X the "
+                               "GEMM reads (the reference's block semantics); " +
+                               ("sharded by rows: each rank normalises 16384/N rows and copies "
+                                "them into every rank's X buffer over NVLink (copy engines); "
+                                if d.world > 1 else "") +
+                               "step i's RMSNorm on a second stream into one of two X buffers, "
+                               "overlapping step i-1's GEMM"),
                    "gemm": "packed GEMM+SwiGLU bf16 out, N-sharded",
                    "parallelism": f"N-shard x{d.world}" if d.world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (X 134 MB, W 235 MB); no flush"},
@@ -658,19 +687,74 @@ def run_ours(args, d: Dist) -> dict | None:
                      "kernel": "gemm_bf16_tc2_kernel (CTA pair, SwiGLU, bf16 out)",
                      "peak_source": f"{pk['source']} {peak_kind} bf16 (timed region "
                                     f"{timed_s * 1e3:.0f} ms)",
-                     "gemm_us_per_launch": round(gemm_us, 2)},
+                     "gemm_us_per_launch": round(gemm_us, 2),
+                     **({"gemm_us_per_launch_ranks": [round(v, 2) for v in gemm_us_ranks]}
+                        if d.world > 1 else {})},
         "cpu_baseline": cpu,
         "parity": parity,
+        **({"sharded_rmsnorm": sharded_norm} if sharded_norm is not None else {}),
         "variants": {**variants, **({"gathered_output": gather} if gather is not None else {})},
         "clocks": clock_info,
-        "gpu_launches": 2 * args.steps,
+        # per step: RMSNorm + GEMM, and at N > 1 the exchange's two barrier kernels
+        "gpu_launches": (2 if d.world == 1 else 4) * args.steps,
         "ops": ops,
     }
+
+
+def pipelined_block(d: Dist, args, x, w_norm, packed, out, rng=None) -> tuple[float, float]:
+    """Times the pipelined block (see run_ours): returns the max over ranks of
+    the timed region (ms) and this rank's mean GEMM launch time (us).  With
+    `rng` (a sharding.RowNormGather) the RMSNorm is row-sharded and
+    all-gathered; without it every rank normalises all rows."""
+    from cuda_operator_lab import bindings as b
+
+    main = torch.cuda.Stream(priority=-1)
+    main.wait_stream(torch.cuda.current_stream())
+    side = torch.cuda.Stream()
+    xns = rng.outputs if rng is not None else [torch.empty_like(x) for _ in range(2)]
+    normed = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    gemm_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
+    step_index = [0]
+
+    def step():
+        j = step_index[0] % 2
+        side.wait_event(consumed[j])  # the GEMM two steps back has read xns[j]
+        with torch.cuda.stream(side):
+            if rng is None:
+                b.rmsnorm_bf16_into(x, w_norm, xns[j], EPS)
+            else:
+                rng(x, w_norm, EPS, slot=j)
+            normed[j].record(side)
+        main.wait_event(normed[j])
+        i = step_index[0] - args.warmup
+        if 0 <= i < args.steps:
+            gemm_events[i][0].record(main)
+        b.gemm_swiglu_bf16_into(xns[j], packed, out)
+        if 0 <= i < args.steps:
+            gemm_events[i][1].record(main)
+        consumed[j].record(main)
+        step_index[0] += 1
+
+    def drain():
+        main.wait_stream(side)
+
+    def start(ev):
+        side.wait_event(ev)
+
+    with torch.cuda.stream(main):
+        ms = time_region(d, step, args.steps, args.warmup, drain=drain, after_start=start)
+    torch.cuda.current_stream().wait_stream(main)
+    gemm_us = 1000.0 * sum(s_.elapsed_time(e_) for s_, e_ in gemm_events) / args.steps
+    return ms, gemm_us
 
 
 def step_variants(d: Dist, args, x, w_norm, packed, out) -> dict:
     """Other forms of the same step, timed in the same run:
 
+    * ``replicated_rmsnorm`` (N > 1): the pipelined step with every rank
+      normalising all rows instead of its row shard;
     * ``serial``: RMSNorm then GEMM on one stream, one normalised-X buffer
       (no overlap between consecutive steps);
     * ``folded``: the RMSNorm folded into the GEMM (a per-row rstd pass, rstd
@@ -680,6 +764,12 @@ def step_variants(d: Dist, args, x, w_norm, packed, out) -> dict:
     from cuda_operator_lab import bindings as b
 
     res = {}
+    if d.world > 1:
+        ms, _ = pipelined_block(d, args, x, w_norm, packed, out, None)
+        res["replicated_rmsnorm"] = {
+            "value": round(GEMM_FLOPS * args.steps / (ms / 1e3) / 1e12, 2),
+            "ms_per_step": round(ms / args.steps, 4),
+            "step": "pipelined like the headline, every rank normalising all 16384 rows"}
     xn = torch.empty_like(x)
 
     def serial():
@@ -710,17 +800,27 @@ def step_variants(d: Dist, args, x, w_norm, packed, out) -> dict:
 
 def e2e_pipeline(d: Dist, args, x, w_norm, packed, out) -> dict:
     """The step through the public API with host buffers: every step copies
-    X from pinned host memory and the output shard back.  Serving-style
-    pipeline: step i's upload (copy stream), RMSNorm + GEMM (this stream)
-    and download (second copy stream) overlap steps i-1 and i+1, with two
-    device and two pinned host buffers.  The serial form (upload, compute,
-    download on one stream) is reported beside it."""
+    X from pinned host memory and the output shard back.  With N ranks each
+    rank uploads only its 1/N of X's rows, normalises them and the copy
+    engines place them in every rank's normalised-X buffer over NVLink
+    (sharding.RowNormGather), so each host byte crosses PCIe once and every
+    row is normalised once.  Serving-style pipeline: step i's upload and
+    RMSNorm (+ exchange) on a copy stream, the GEMM on this stream and the
+    download on a second copy stream overlap steps i-1 and i+1, with two
+    device and two pinned host buffers.  The serial form (all of it on one
+    stream) is reported beside it."""
     from cuda_operator_lab import bindings as b
+    from cuda_operator_lab import sharding
 
-    x_host = x.cpu().pin_memory()
+    world = d.world
+    if M % world:
+        raise SystemExit(f"M={M} must divide evenly between {world} ranks")
+    rows = M // world
+    x_host = x[d.rank * rows:(d.rank + 1) * rows].cpu().pin_memory()
     out_host = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
-    x_dev = [torch.empty_like(x) for _ in range(2)]
-    xn_dev = [torch.empty_like(x) for _ in range(2)]
+    x_dev = [torch.empty(rows, K, device=x.device, dtype=x.dtype) for _ in range(2)]
+    rng = sharding.RowNormGather(M, K) if world > 1 else None
+    xn_dev = rng.outputs if rng is not None else [torch.empty_like(x) for _ in range(2)]
     out_dev = [out, torch.empty_like(out)]
     main = torch.cuda.current_stream()
     up, down = torch.cuda.Stream(), torch.cuda.Stream()
@@ -729,16 +829,24 @@ def e2e_pipeline(d: Dist, args, x, w_norm, packed, out) -> dict:
     downloaded = [torch.cuda.Event() for _ in range(2)]
     index = [0]
 
+    def upload_norm(j):
+        """On the current stream: this rank's rows of X in, all rows normalised
+        into xn_dev[j]."""
+        x_dev[j].copy_(x_host, non_blocking=True)
+        if rng is None:
+            b.rmsnorm_bf16_into(x_dev[j], w_norm, xn_dev[j], EPS)
+        else:
+            rng(x_dev[j], w_norm, EPS, slot=j)
+
     def e2e_step():
         j = index[0] % 2
         index[0] += 1
         with torch.cuda.stream(up):
-            up.wait_event(computed[j])  # step i-2 has finished reading x_dev[j]
-            x_dev[j].copy_(x_host, non_blocking=True)
+            up.wait_event(computed[j])  # step i-2's GEMM has read xn_dev[j]
+            upload_norm(j)
             uploaded[j].record(up)
         main.wait_event(uploaded[j])
         main.wait_event(downloaded[j])  # step i-2's output has left out_dev[j]
-        b.rmsnorm_bf16_into(x_dev[j], w_norm, xn_dev[j], EPS)
         b.gemm_swiglu_bf16_into(xn_dev[j], packed, out_dev[j])
         computed[j].record(main)
         with torch.cuda.stream(down):
@@ -749,10 +857,10 @@ def e2e_pipeline(d: Dist, args, x, w_norm, packed, out) -> dict:
     def drain():
         for ev in downloaded:
             main.wait_event(ev)
+        main.wait_stream(up)
 
     def serial_step():
-        x_dev[0].copy_(x_host, non_blocking=True)
-        b.rmsnorm_bf16_into(x_dev[0], w_norm, xn_dev[0], EPS)
+        upload_norm(0)
         b.gemm_swiglu_bf16_into(xn_dev[0], packed, out)
         out_host[0].copy_(out, non_blocking=True)
 
@@ -762,15 +870,29 @@ def e2e_pipeline(d: Dist, args, x, w_norm, packed, out) -> dict:
         up.wait_event(ev)
         down.wait_event(ev)
 
-    e2e_ms = time_region(d, e2e_step, steps, 2, drain=drain, after_start=start)
-    last = (index[0] - 1) % 2
-    torch.testing.assert_close(out_host[last][:4].float(), out_dev[last][:4].cpu().float())
-    serial_ms = time_region(d, serial_step, steps, 2)
-    torch.testing.assert_close(out_host[0][:4].float(), out[:4].cpu().float())
+    try:
+        e2e_ms = time_region(d, e2e_step, steps, 2, drain=drain, after_start=start)
+        last = (index[0] - 1) % 2
+        torch.testing.assert_close(out_host[last][:4].float(), out_dev[last][:4].cpu().float())
+        # the normalised X assembled from every rank's upload is the RMSNorm of X
+        assert torch.equal(xn_dev[last], b.rmsnorm_bf16(x, w_norm, EPS)), \
+            "normalised X assembled from the uploads differs"
+        serial_ms = time_region(d, serial_step, steps, 2)
+        torch.testing.assert_close(out_host[0][:4].float(), out[:4].cpu().float())
+        if rng is not None:
+            rng.check()
+    finally:
+        if rng is not None:
+            del xn_dev
+            rng.close()
     return {"value": round(GEMM_FLOPS * steps / (e2e_ms / 1e3) / 1e12, 2),
-            "unit": "TFLOP/s", "h2d_bytes_per_step": M * K * 2 * d.world,
-            "d2h_bytes_per_step": M * N * 2,
-            "pipeline": "upload / RMSNorm+GEMM / download on three streams, two buffers",
+            "unit": "TFLOP/s",
+            # whole job: each rank copies its rows of X in and its output columns out
+            "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+            "pipeline": ("upload of this rank's rows of X + their RMSNorm + copy-engine "
+                         "exchange of the normalised rows over NVLink / GEMM / download on "
+                         "three streams, two buffers")
+            if world > 1 else "upload + RMSNorm / GEMM / download on three streams, two buffers",
             "serial_value": round(GEMM_FLOPS * steps / (serial_ms / 1e3) / 1e12, 2)}
 
 

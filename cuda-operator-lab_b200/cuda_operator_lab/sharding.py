@@ -305,3 +305,165 @@ class PeerColumnGather:
         for addr in self._local:
             self.peers.free(addr)
         self._local = None
+
+
+# ---------------------------------------------------------------- row-sharded norm, all-gathered
+
+
+def _library_rmsnorm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, eps: float) -> None:
+    from . import bindings
+
+    bindings.rmsnorm_bf16_into(x, weight, out, eps)
+
+
+class RowNormGather:
+    """bf16 RMSNorm of X[M, K] sharded by rows, the normalised rows
+    all-gathered to every rank over NVLink by the copy engines.
+
+    The large MLP workload needs the whole normalised X on every rank (each
+    rank's GEMM owns an N slice, all M rows).  Instead of every rank
+    normalising all M rows, rank r normalises its M/g rows straight into its
+    own [M, K] buffer and copies them into the same rows of every other rank's
+    buffer (memory mapped with CUDA IPC; one ``cudaMemcpyAsync`` per peer on
+    its own stream, so the copies run on the copy engines in parallel and use
+    no SMs).  Two device flag barriers bracket a call: the first makes sure no
+    rank still reads the buffer (its previous use), the second that every
+    rank's rows have landed.  Run on a second stream, a call overlaps the
+    previous step's GEMM: the copies take the NVLink and HBM bandwidth the
+    tensor-core GEMM leaves idle.
+
+    Two buffers alternate (``slot``).  Before a call the caller must have
+    ordered, on the current stream, every read of that slot's previous
+    contents on this rank; the first barrier extends that to all ranks.
+    Construction and :meth:`close` are collective; ``peers`` supplies memory,
+    views and the barrier (default: the CUDA library), ``norm`` the per-shard
+    RMSNorm (default: ``bindings.rmsnorm_bf16_into``).  The barriers wait a
+    bounded time; :meth:`check` raises if one gave up.
+    """
+
+    def __init__(self, m: int, k: int, group=None, peers=None,
+                 norm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor, float], None] | None = None
+                 ) -> None:
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if not 1 <= self.world <= 8:
+            raise ValueError("the row-sharded norm gather supports 1 to 8 ranks")
+        if m % self.world:
+            raise ValueError("M must divide evenly between the ranks")
+        self.m, self.k, self.rows = m, k, m // self.world
+        self.group = group
+        self.peers = peers if peers is not None else LibraryPeers()
+        self.norm = norm if norm is not None else _library_rmsnorm
+        buf_bytes = m * k * 2
+        self._flag_offset = -(-buf_bytes // 256) * 256
+        nbytes = self._flag_offset + _FLAG_BYTES
+        self._local: list[int] | None = []
+        self._opened: list[int] = []
+        handles: list[bytes] = []
+        try:
+            for _ in range(2):
+                addr, handle = self.peers.alloc(nbytes)
+                self._local.append(addr)
+                handles.append(handle)
+            every = [None] * self.world
+            if self.world > 1:
+                dist.all_gather_object(every, handles, group=group)
+            else:
+                every = [handles]
+            self.addrs = [[0] * self.world for _ in range(2)]
+            for j in range(self.world):
+                for i in range(2):
+                    if j == self.rank:
+                        self.addrs[i][j] = self._local[i]
+                    else:
+                        self.addrs[i][j] = self.peers.open(every[j][i])
+                        self._opened.append(self.addrs[i][j])
+        except Exception:
+            for addr in self._opened:
+                self.peers.close(addr)
+            for addr in self._local:
+                self.peers.free(addr)
+            self._local = None
+            raise
+        self.outputs = [self.peers.view(self._local[i], m, k) for i in range(2)]
+        row_bytes = self.rank * self.rows * k * 2
+        # dests[i][j]: this rank's rows inside rank j's buffer i, as mapped here
+        self.dests = [[self.peers.view(self.addrs[i][j] + row_bytes, self.rows, k)
+                       for j in range(self.world)] for i in range(2)]
+        self.flag_addrs = [self.addrs[0][j] + self._flag_offset for j in range(self.world)]
+        self.epoch = 0
+        self.calls = 0
+        self._streams = None
+        if torch.cuda.is_available() and self.outputs[0].is_cuda:
+            self._streams = [torch.cuda.Stream() for _ in range(self.world)]
+        if self.world > 1:
+            dist.barrier(group=group)  # every mapping exists before any copy
+
+    def _barrier(self) -> None:
+        self.epoch += 1
+        self.peers.barrier(self.flag_addrs, self.rank, self.epoch)
+
+    def __call__(self, x: torch.Tensor, weight: torch.Tensor, eps: float,
+                 slot: int | None = None) -> torch.Tensor:
+        """RMSNorm of every row of X (bf16), this rank computing its M/g rows.
+        `x` is either the whole X [M, K] or only this rank's rows [M/g, K]
+        (rows r*M/g to (r+1)*M/g - 1).  Returns buffer `slot` (default:
+        alternating) holding all M normalised rows once the current stream
+        reaches it."""
+        lo = self.rank * self.rows
+        if tuple(x.shape) == (self.m, self.k):
+            x = x[lo:lo + self.rows]
+        elif tuple(x.shape) != (self.rows, self.k):
+            raise ValueError(f"expected x[{self.m}, {self.k}] or this rank's rows "
+                             f"x[{self.rows}, {self.k}]")
+        i = self.calls % 2 if slot is None else slot
+        if i not in (0, 1):
+            raise ValueError("slot must be 0 or 1")
+        self.calls += 1
+        self._barrier()  # nobody still reads buffer i
+        own = self.outputs[i][lo:lo + self.rows]
+        self.norm(x, weight, own, eps)
+        if self.world > 1:
+            if self._streams is not None:
+                current = torch.cuda.current_stream()
+                for j in range(self.world):
+                    if j == self.rank:
+                        continue
+                    s = self._streams[j]
+                    s.wait_stream(current)
+                    with torch.cuda.stream(s):
+                        self.dests[i][j].copy_(own, non_blocking=True)
+                for j in range(self.world):
+                    if j != self.rank:
+                        current.wait_stream(self._streams[j])
+            else:
+                for j in range(self.world):
+                    if j != self.rank:
+                        self.dests[i][j].copy_(own)
+        self._barrier()  # every rank's rows have landed
+        return self.outputs[i]
+
+    def check(self) -> None:
+        """Raise RuntimeError if a barrier of an earlier call gave up waiting
+        (a buffer may then miss other ranks' rows).  Synchronises the device."""
+        code = self.peers.status()
+        if code != 0:
+            raise RuntimeError(f"row-sharded norm gather: a peer barrier timed out (status {code})")
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (collective)."""
+        if self._local is None:
+            return
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self.dests = []
+        for addr in self._opened:
+            self.peers.close(addr)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self.outputs = []
+        for addr in self._local:
+            self.peers.free(addr)
+        self._local = None

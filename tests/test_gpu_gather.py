@@ -8,6 +8,9 @@ and for a wait that runs out (a flag that nothing sets: the kernel must give
 up after its limit, report it in the peer status word and leave the context
 usable).  With two or more GPUs, ranks in separate processes exchange CUDA
 IPC handles and gather over NVLink through ``sharding.PeerColumnGather``.
+The row-sharded RMSNorm with its copy-engine all-gather
+(``sharding.RowNormGather``) runs as one rank here and across every GPU the
+box has, in both cases bit for bit against the unsharded RMSNorm.
 """
 
 from __future__ import annotations
@@ -220,5 +223,86 @@ def test_peer_column_gather_across_gpus(layout):
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()
     mp.start_processes(_ranks_worker, args=(world, _free_port(), results, layout),
+                       nprocs=world, join=True, start_method="spawn")
+    assert dict(results) == {r: (True, 0, 0) for r in range(world)}
+
+
+# ---------------------------------------------------------------- row-sharded RMSNorm + all-gather
+
+
+def _row_norm_case(rng, rank, world, m, k, pipelined):
+    """Six calls of the row-sharded RMSNorm (whole X and own rows alternating),
+    each output against the unsharded bf16 RMSNorm bit for bit and fed to a
+    GEMM; in the pipelined form the calls run on a side stream while the
+    previous call's GEMM runs, ordered by events as in the benchmark."""
+    g = seeded(555)
+    w = (torch.rand(k, generator=g) + 0.5).to(torch.bfloat16).to(DEV)
+    packed = (torch.randn(2 * 128, k, generator=g) * k ** -0.5).to(torch.bfloat16).to(DEV)
+    xs = [torch.randn(m, k, generator=g).to(torch.bfloat16).to(DEV) for _ in range(6)]
+    rows = m // world
+    main = torch.cuda.current_stream()
+    side = torch.cuda.Stream() if pipelined else main
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    outs = []
+    for call, x in enumerate(xs):
+        j = call % 2
+        side.wait_event(consumed[j])
+        with torch.cuda.stream(side):
+            arg = x if call % 2 == 0 else x[rank * rows:(rank + 1) * rows]
+            xn = rng(arg, w, 1e-6, slot=j)
+            normed = torch.cuda.Event()
+            normed.record(side)
+        main.wait_event(normed)
+        outs.append((xn.clone(), b.gemm_swiglu_bf16(xn, packed)))
+        consumed[j].record(main)
+    ok = True
+    for x, (xn, y) in zip(xs, outs):
+        expected = b.rmsnorm_bf16(x, w, 1e-6)
+        ok = ok and torch.equal(xn, expected)
+        ok = ok and torch.equal(y, b.gemm_swiglu_bf16(expected, packed))
+    rng.check()
+    return ok
+
+
+def test_row_norm_gather_one_rank():
+    rng = sharding.RowNormGather(384, 4096)
+    try:
+        assert _row_norm_case(rng, 0, 1, 384, 4096, pipelined=True)
+    finally:
+        rng.close()
+    assert b.peer_status(clear=True) == 0
+
+
+def _row_norm_worker(rank: int, world: int, port: int, results) -> None:
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    rng = None
+    try:
+        m, k = 136 * world, 4096  # 136 rows per rank: not a multiple of a CTA's rows
+        rng = sharding.RowNormGather(m, k)
+        ok = _row_norm_case(rng, rank, world, m, k, pipelined=False)
+        ok = _row_norm_case(rng, rank, world, m, k, pipelined=True) and ok
+        results[rank] = (ok, b.peer_status(), b.gemm_status())
+    finally:
+        if rng is not None:
+            rng.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_row_norm_gather_across_gpus():
+    """Each rank normalises its rows of X and the copy engines place them in
+    every rank's buffer over NVLink: every rank's buffer must equal the
+    unsharded RMSNorm bit for bit after every call."""
+    world = min(torch.cuda.device_count(), 8)
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_row_norm_worker, args=(world, _free_port(), results),
                        nprocs=world, join=True, start_method="spawn")
     assert dict(results) == {r: (True, 0, 0) for r in range(world)}

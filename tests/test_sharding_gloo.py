@@ -218,6 +218,67 @@ def test_peer_column_gather_two_gloo_ranks(layout):
     assert dict(results) == {r: (True, True, True, True, True) for r in range(world)}
 
 
+def _row_norm_worker(rank: int, world: int, port: int, results) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = torch.Generator()
+        g.manual_seed(8765)
+        m, k = 16, 40
+        xs = [torch.randn(m, k, generator=g).to(torch.bfloat16) for _ in range(3)]
+        w = (torch.rand(k, generator=g) + 0.5).to(torch.bfloat16)
+        normed_rows = []
+
+        def norm(x, weight, out, eps):
+            normed_rows.append(x.shape[0])
+            out.copy_(oracle.rmsnorm_bf16(x, weight, eps))
+
+        peers = HostPeers()
+        rng = sharding.RowNormGather(m, k, peers=peers, norm=norm)
+        rows = m // world
+        ok, ptrs = [], []
+        for call, x in enumerate(xs):
+            # whole X on even calls, only this rank's rows on odd ones
+            arg = x if call % 2 == 0 else x[rank * rows:(rank + 1) * rows]
+            out = rng(arg, w, 1e-6)
+            dist.barrier()  # the host stand-in copies synchronously: every rank done
+            ok.append(torch.equal(out, oracle.rmsnorm_bf16(x, w, 1e-6)))
+            ptrs.append(out.data_ptr())
+            dist.barrier()  # every rank checked before the buffer is reused
+        alternate = ptrs[0] == ptrs[2] != ptrs[1]
+        own_rows_only = normed_rows == [rows] * 3
+        epochs = peers.epochs_seen == [True] * 6 and rng.epoch == 6
+        del out
+        rng.close()
+        results[rank] = (all(ok), alternate, own_rows_only, epochs, not peers.segments)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_row_norm_gather_gloo_ranks(world):
+    """Host logic of the row-sharded RMSNorm with its all-gather: each rank
+    normalises only its M/g rows, its rows land in every rank's buffer, two
+    barrier epochs per call, alternating buffers, collective close."""
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_row_norm_worker, args=(world, _free_port(), results),
+                       nprocs=world, join=True, start_method="spawn")
+    assert dict(results) == {r: (True, True, True, True, True) for r in range(world)}
+
+
+def test_row_norm_gather_rejects_bad_shapes():
+    peers = HostPeers()
+    rng = sharding.RowNormGather(8, 16, peers=peers, norm=lambda *a: None)
+    with pytest.raises(ValueError):
+        rng(torch.zeros(4, 8, dtype=torch.bfloat16), torch.zeros(16), 1e-6)
+    with pytest.raises(ValueError):
+        rng(torch.zeros(8, 16, dtype=torch.bfloat16), torch.zeros(16), 1e-6, slot=2)
+    rng.close()
+    assert not peers.segments
+
+
 def test_peer_column_gather_rejects_bad_shapes():
     peers = HostPeers()
     gather = sharding.PeerColumnGather(8, 20, peers=peers)
