@@ -7,8 +7,8 @@ TFLOP/s for the whole job.  One step = the block as the reference defines it:
 the bf16 RMSNorm of all rows (each rank needs the whole normalised X for its N
 slice) writing the normalised X, then the N-sharded GEMM+SwiGLU with bf16
 output.  With N > 1 ranks the RMSNorm is sharded by rows: each rank
-normalises M/N rows and the copy engines copy them into every rank's X buffer
-over NVLink.  Consecutive steps are pipelined over two normalised-X buffers:
+normalises M/N rows and its norm kernel stores them into every rank's X
+buffer over NVLink (peer stores, then a device flag barrier).  Consecutive steps are pipelined over two normalised-X buffers:
 step i's RMSNorm (and exchange) runs on a second stream and overlaps step
 i-1's GEMM.  All inputs
 are resident in HBM (X 134 MB and W 235 MB exceed the 126 MB L2, so no flush
@@ -571,9 +571,9 @@ def run_ours(args, d: Dist) -> dict | None:
     # row of X (each rank needs all rows for its N slice) writing normalised X,
     # then the packed GEMM+SwiGLU of this rank's N slice.  With N ranks the
     # RMSNorm is sharded by rows: each rank normalises its M/N rows and the
-    # copy engines push them into every peer's buffer over NVLink
-    # (sharding.RowNormGather), so no rank repeats the others' work and no SM
-    # is spent on the exchange.  Steps are pipelined over two normalised-X
+    # norm kernel stores them into every peer's buffer over NVLink
+    # (sharding.RowNormGather), so no rank repeats the others' work.  Steps
+    # are pipelined over two normalised-X
     # buffers: step i's RMSNorm (and exchange) runs on a second stream as soon
     # as the GEMM two steps back has read its buffer -- on every rank, by the
     # exchange's first barrier -- so it overlaps the previous GEMM; step i's
@@ -591,7 +591,8 @@ def run_ours(args, d: Dist) -> dict | None:
         rng = sharding.RowNormGather(M, K)
     try:
         with ClockSampler(physical_gpus(d.world), enabled=d.rank == 0) as clocks:
-            ms, gemm_rank_us = pipelined_block(d, args, x, w_norm, packed, out, rng)
+            norm = (lambda j: rng(x, w_norm, EPS, slot=j)) if rng is not None else None
+            ms, gemm_rank_us = pipelined_block(d, args, x, w_norm, packed, out, norm)
         step_ms_ranks = [v / args.steps for v in d.last_region_ms]
         sharded_norm = None
         if rng is not None:
@@ -602,8 +603,9 @@ def run_ours(args, d: Dist) -> dict | None:
                 "identical_to_unsharded": d.max(0.0 if same else 1.0) == 0.0,
                 "rows_per_rank": M // d.world,
                 "nvlink_bytes_per_rank": (d.world - 1) * (M // d.world) * K * 2,
-                "exchange": "cudaMemcpyAsync per peer into its CUDA IPC buffer (copy "
-                            "engines), two device flag barriers per step"}
+                "exchange": "rmsnorm_allgather_bf16: the norm kernel stores each row into "
+                            "every rank's CUDA IPC buffer over NVLink; two device flag "
+                            "barriers per step"}
     finally:
         if rng is not None:
             rng.close()
@@ -669,9 +671,9 @@ def run_ours(args, d: Dist) -> dict | None:
         "config": {"workload": "llama_mlp_block (BASELINE config 5)", "M": M, "K": K, "N": N,
                    "rmsnorm": ("bf16 RMSNorm of all 16384 rows writing the normalised X the "
                                "GEMM reads (the reference's block semantics); " +
-                               ("sharded by rows: each rank normalises 16384/N rows and copies "
-                                "them into every rank's X buffer over NVLink (copy engines); "
-                                if d.world > 1 else "") +
+                               ("sharded by rows: each rank normalises 16384/N rows and its "
+                                "norm kernel stores them into every rank's X buffer over "
+                                "NVLink; " if d.world > 1 else "") +
                                "step i's RMSNorm on a second stream into one of two X buffers, "
                                "overlapping step i-1's GEMM"),
                    "gemm": "packed GEMM+SwiGLU bf16 out, N-sharded",
@@ -701,17 +703,50 @@ def run_ours(args, d: Dist) -> dict | None:
     }
 
 
-def pipelined_block(d: Dist, args, x, w_norm, packed, out, rng=None) -> tuple[float, float]:
+def norm_replicated(x, w_norm):
+    """Every rank normalises all rows into one of two buffers."""
+    from cuda_operator_lab import bindings as b
+
+    xns = [torch.empty_like(x) for _ in range(2)]
+
+    def norm(j):
+        b.rmsnorm_bf16_into(x, w_norm, xns[j], EPS)
+        return xns[j]
+    return norm
+
+
+def norm_nccl(d: Dist, x, w_norm):
+    """Each rank normalises its rows; NCCL all-gathers them into one of two
+    full buffers."""
+    from cuda_operator_lab import bindings as b
+
+    rows = M // d.world
+    lo = d.rank * rows
+    parts = [torch.empty(rows, K, device=x.device, dtype=x.dtype) for _ in range(2)]
+    xns = [torch.empty_like(x) for _ in range(2)]
+
+    def norm(j):
+        b.rmsnorm_bf16_into(x[lo:lo + rows], w_norm, parts[j], EPS)
+        d.dist.all_gather_into_tensor(xns[j], parts[j])
+        return xns[j]
+    return norm
+
+
+def pipelined_block(d: Dist, args, x, w_norm, packed, out, norm=None) -> tuple[float, float]:
     """Times the pipelined block (see run_ours): returns the max over ranks of
-    the timed region (ms) and this rank's mean GEMM launch time (us).  With
-    `rng` (a sharding.RowNormGather) the RMSNorm is row-sharded and
-    all-gathered; without it every rank normalises all rows."""
+    the timed region (ms) and this rank's mean GEMM launch time (us).
+    `norm(slot)` enqueues, on the current (second) stream, the RMSNorm of all
+    rows into buffer `slot` and returns that buffer: a row-sharded
+    sharding.RowNormGather, or a replicated or NCCL form (default:
+    replicated)."""
     from cuda_operator_lab import bindings as b
 
     main = torch.cuda.Stream(priority=-1)
     main.wait_stream(torch.cuda.current_stream())
     side = torch.cuda.Stream()
-    xns = rng.outputs if rng is not None else [torch.empty_like(x) for _ in range(2)]
+    if norm is None:
+        norm = norm_replicated(x, w_norm)
+    xns = [None, None]
     normed = [torch.cuda.Event() for _ in range(2)]
     consumed = [torch.cuda.Event() for _ in range(2)]
     gemm_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -722,10 +757,7 @@ def pipelined_block(d: Dist, args, x, w_norm, packed, out, rng=None) -> tuple[fl
         j = step_index[0] % 2
         side.wait_event(consumed[j])  # the GEMM two steps back has read xns[j]
         with torch.cuda.stream(side):
-            if rng is None:
-                b.rmsnorm_bf16_into(x, w_norm, xns[j], EPS)
-            else:
-                rng(x, w_norm, EPS, slot=j)
+            xns[j] = norm(j)
             normed[j].record(side)
         main.wait_event(normed[j])
         i = step_index[0] - args.warmup
@@ -753,8 +785,10 @@ def pipelined_block(d: Dist, args, x, w_norm, packed, out, rng=None) -> tuple[fl
 def step_variants(d: Dist, args, x, w_norm, packed, out) -> dict:
     """Other forms of the same step, timed in the same run:
 
-    * ``replicated_rmsnorm`` (N > 1): the pipelined step with every rank
-      normalising all rows instead of its row shard;
+    * ``replicated_rmsnorm``, ``nccl_rmsnorm_allgather`` and
+      ``copy_engine_rmsnorm_allgather`` (N > 1): the pipelined step with every
+      rank normalising all rows, or its rows all-gathered by NCCL or by the
+      copy engines, instead of the headline's peer stores from the norm kernel;
     * ``serial``: RMSNorm then GEMM on one stream, one normalised-X buffer
       (no overlap between consecutive steps);
     * ``folded``: the RMSNorm folded into the GEMM (a per-row rstd pass, rstd
@@ -763,13 +797,32 @@ def step_variants(d: Dist, args, x, w_norm, packed, out) -> dict:
       X, so it is not the reference's block bit for bit."""
     from cuda_operator_lab import bindings as b
 
+    from cuda_operator_lab import sharding
+
     res = {}
+
+    def entry(ms, text):
+        return {"value": round(GEMM_FLOPS * args.steps / (ms / 1e3) / 1e12, 2),
+                "ms_per_step": round(ms / args.steps, 4), "step": text}
+
     if d.world > 1:
         ms, _ = pipelined_block(d, args, x, w_norm, packed, out, None)
-        res["replicated_rmsnorm"] = {
-            "value": round(GEMM_FLOPS * args.steps / (ms / 1e3) / 1e12, 2),
-            "ms_per_step": round(ms / args.steps, 4),
-            "step": "pipelined like the headline, every rank normalising all 16384 rows"}
+        res["replicated_rmsnorm"] = entry(
+            ms, "pipelined like the headline, every rank normalising all 16384 rows")
+        ms, _ = pipelined_block(d, args, x, w_norm, packed, out, norm_nccl(d, x, w_norm))
+        res["nccl_rmsnorm_allgather"] = entry(
+            ms, "pipelined like the headline, each rank normalising its rows, NCCL "
+                "all_gather_into_tensor of the normalised rows on the second stream")
+        rng = sharding.RowNormGather(M, K, exchange="copies")
+        try:
+            ms, _ = pipelined_block(d, args, x, w_norm, packed, out,
+                                    lambda j: rng(x, w_norm, EPS, slot=j))
+            rng.check()
+        finally:
+            rng.close()
+        res["copy_engine_rmsnorm_allgather"] = entry(
+            ms, "pipelined like the headline, each rank normalising its rows into its own "
+                "buffer, one cudaMemcpyAsync per peer (copy engines) between the barriers")
     xn = torch.empty_like(x)
 
     def serial():
@@ -801,8 +854,8 @@ def step_variants(d: Dist, args, x, w_norm, packed, out) -> dict:
 def e2e_pipeline(d: Dist, args, x, w_norm, packed, out) -> dict:
     """The step through the public API with host buffers: every step copies
     X from pinned host memory and the output shard back.  With N ranks each
-    rank uploads only its 1/N of X's rows, normalises them and the copy
-    engines place them in every rank's normalised-X buffer over NVLink
+    rank uploads only its 1/N of X's rows, normalises them and the norm
+    kernel stores them into every rank's normalised-X buffer over NVLink
     (sharding.RowNormGather), so each host byte crosses PCIe once and every
     row is normalised once.  Serving-style pipeline: step i's upload and
     RMSNorm (+ exchange) on a copy stream, the GEMM on this stream and the
@@ -889,9 +942,9 @@ def e2e_pipeline(d: Dist, args, x, w_norm, packed, out) -> dict:
             "unit": "TFLOP/s",
             # whole job: each rank copies its rows of X in and its output columns out
             "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
-            "pipeline": ("upload of this rank's rows of X + their RMSNorm + copy-engine "
-                         "exchange of the normalised rows over NVLink / GEMM / download on "
-                         "three streams, two buffers")
+            "pipeline": ("upload of this rank's rows of X + their RMSNorm, stored by the "
+                         "norm kernel into every rank's X buffer over NVLink / GEMM / "
+                         "download on three streams, two buffers")
             if world > 1 else "upload + RMSNorm / GEMM / download on three streams, two buffers",
             "serial_value": round(GEMM_FLOPS * steps / (serial_ms / 1e3) / 1e12, 2)}
 

@@ -77,6 +77,7 @@ _SIGNATURES["cuda_operator_rmsnorm_rstd_bf16"] = [_P, _P, _U64, _U64, _F32, _P]
 _SIGNATURES["cuda_operator_gemm_swiglu_rowscale_bf16"] = [_P, _P, _P, _P, _U64, _U64, _U64, _P]
 _SIGNATURES["cuda_operator_gemm_swiglu_allgather_bf16"] = [
     _P, _P, _P, _P, _I32, _U64, _U64, _U64, _U64, _P]
+_SIGNATURES["cuda_operator_rmsnorm_allgather_bf16"] = [_P, _P, _P, _I32, _U64, _U64, _F32, _P]
 _SIGNATURES["cuda_operator_reduction_partial_f64"] = [_P, _P, _U64, _P]
 _SIGNATURES["cuda_operator_lab_peer_handle_bytes"] = []
 _SIGNATURES["cuda_operator_lab_peer_alloc"] = [_U64, _P, _P]
@@ -918,6 +919,36 @@ def gemm_swiglu_allgather_bf16(x_bf16: torch.Tensor, row_scale: torch.Tensor | N
           int(k), int(n), int(ld), _stream(x_bf16))
 
 
+def rmsnorm_allgather_bf16(x_bf16: torch.Tensor, weight_bf16: torch.Tensor,
+                           dests: Sequence[int], eps: float = 1e-5) -> None:
+    """bf16 RMSNorm of x [rows, cols] (bit for bit :func:`rmsnorm_bf16`) stored
+    to every address in ``dests``: each is where these rows go in a bf16
+    buffer with row stride cols -- this GPU's first, then the other ranks' as
+    mapped by :func:`peer_open`.  Enqueued on the current stream of x's device;
+    follow it with :func:`peer_barrier` before other ranks read the rows.
+    cols must be a multiple of 8 and at most 8192."""
+    if not _all_cuda(x_bf16, weight_bf16):
+        raise ValueError("RMSNorm tensors must be CUDA tensors")
+    if x_bf16.ndim != 2 or weight_bf16.ndim != 1 or weight_bf16.shape[0] != x_bf16.shape[1]:
+        raise ValueError("expected x [rows, cols] and a weight of cols elements")
+    if x_bf16.dtype != torch.bfloat16 or weight_bf16.dtype != torch.bfloat16:
+        raise TypeError("RMSNorm all-gather expects bfloat16 x and weight")
+    if not _all_contiguous(x_bf16, weight_bf16):
+        raise ValueError("RMSNorm tensors must be contiguous")
+    if x_bf16.shape[1] % 8 or x_bf16.shape[1] > 8192:
+        raise ValueError("cols must be a multiple of 8 and at most 8192")
+    if not 1 <= len(dests) <= 8 or any(int(d) == 0 for d in dests):
+        raise ValueError("dests must hold 1 to 8 non-null device addresses")
+    if eps <= 0:
+        raise ValueError("eps must be positive")
+    rows, cols = x_bf16.shape
+    if rows == 0:
+        return
+    array = (ctypes.c_void_p * len(dests))(*[int(d) for d in dests])
+    _call("cuda_operator_rmsnorm_allgather_bf16", _ptr(x_bf16), _ptr(weight_bf16), array,
+          int(len(dests)), int(rows), int(cols), float(eps), _stream(x_bf16))
+
+
 def peer_alloc(nbytes: int) -> tuple[int, bytes]:
     """Zero-filled device allocation on the current device that other processes
     can map: (address, handle bytes to send them)."""
@@ -972,7 +1003,7 @@ def peer_status(clear: bool = True) -> int:
     return int(value.value)
 
 
-__all__ += ["gemm_swiglu_allgather_bf16", "peer_alloc", "peer_open", "peer_close", "peer_free",
+__all__ += ["gemm_swiglu_allgather_bf16", "rmsnorm_allgather_bf16", "peer_alloc", "peer_open", "peer_close", "peer_free",
             "peer_barrier", "peer_status"]
 
 # ---------------------------------------------------------------- GEMM + SwiGLU
@@ -1030,6 +1061,25 @@ def _make_gemm_swiglu_packed(version: int, in_dtype: torch.dtype, ws_dtype: torc
 
     def into(x: torch.Tensor, packed_weight: torch.Tensor, workspace: torch.Tensor,
              out: torch.Tensor) -> torch.Tensor:
+        # Fast path: every check below in one expression, each attribute read
+        # once (a small GEMM's call is host-bound).  Anything it rejects goes
+        # through the checks in the reference's order for the exact error.
+        xs, ps = x.shape, packed_weight.shape
+        if (len(xs) == 2 and len(ps) == 2 and xs[1] == ps[1] and not ps[0] & 1
+                and x.dtype is in_dtype and packed_weight.dtype is in_dtype
+                and workspace.dtype is ws_dtype and out.dtype is torch.float32
+                and x.is_cuda and packed_weight.is_cuda and workspace.is_cuda and out.is_cuda
+                and workspace.shape == (xs[0], ps[0]) and out.shape == (xs[0], ps[0] >> 1)
+                and x.is_contiguous() and packed_weight.is_contiguous()
+                and workspace.is_contiguous() and out.is_contiguous()):
+            if xs[0] and ps[0]:
+                _call(symbol, x.data_ptr(), packed_weight.data_ptr(), workspace.data_ptr(),
+                      out.data_ptr(), xs[0], xs[1], ps[0] >> 1, _stream(x))
+            return out
+        return checked_into(x, packed_weight, workspace, out)
+
+    def checked_into(x: torch.Tensor, packed_weight: torch.Tensor, workspace: torch.Tensor,
+                     out: torch.Tensor) -> torch.Tensor:
         if not _all_cuda(x, packed_weight, workspace, out):
             raise ValueError(f"GEMM SwiGLU {tag} tensors must be CUDA tensors")
         if x.ndim != 2 or packed_weight.ndim != 2:

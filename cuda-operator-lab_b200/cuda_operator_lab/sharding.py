@@ -118,10 +118,11 @@ class _CudaWords:
 
 
 class LibraryPeers:
-    """Peer memory, fused gather GEMM and barrier of the CUDA library.
+    """Peer memory, fused gather GEMM and RMSNorm, and barrier of the CUDA
+    library.
 
-    The operations :class:`PeerColumnGather` needs, as one object so that a
-    test can substitute host-side stand-ins for them."""
+    The operations :class:`PeerColumnGather` and :class:`RowNormGather` need,
+    as one object so that a test can substitute host-side stand-ins for them."""
 
     def __init__(self, timeout_ns: int = 5_000_000_000) -> None:
         from . import bindings
@@ -147,6 +148,10 @@ class LibraryPeers:
     def gemm(self, x: torch.Tensor, row_scale: torch.Tensor | None, packed_shard: torch.Tensor,
              dests: Sequence[int], ld: int) -> None:
         self._b.gemm_swiglu_allgather_bf16(x, row_scale, packed_shard, dests, ld)
+
+    def rmsnorm_gather(self, x: torch.Tensor, weight: torch.Tensor, dests: Sequence[int],
+                       eps: float) -> None:
+        self._b.rmsnorm_allgather_bf16(x, weight, dests, eps)
 
     def barrier(self, flag_addrs: Sequence[int], rank: int, epoch: int) -> None:
         self._b.peer_barrier(flag_addrs, rank, epoch, self.timeout_ns)
@@ -318,32 +323,41 @@ def _library_rmsnorm(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, e
 
 class RowNormGather:
     """bf16 RMSNorm of X[M, K] sharded by rows, the normalised rows
-    all-gathered to every rank over NVLink by the copy engines.
+    all-gathered to every rank over NVLink.
 
     The large MLP workload needs the whole normalised X on every rank (each
     rank's GEMM owns an N slice, all M rows).  Instead of every rank
-    normalising all M rows, rank r normalises its M/g rows straight into its
-    own [M, K] buffer and copies them into the same rows of every other rank's
-    buffer (memory mapped with CUDA IPC; one ``cudaMemcpyAsync`` per peer on
-    its own stream, so the copies run on the copy engines in parallel and use
-    no SMs).  Two device flag barriers bracket a call: the first makes sure no
-    rank still reads the buffer (its previous use), the second that every
-    rank's rows have landed.  Run on a second stream, a call overlaps the
-    previous step's GEMM: the copies take the NVLink and HBM bandwidth the
-    tensor-core GEMM leaves idle.
+    normalising all M rows, rank r normalises its M/g rows and places them in
+    the same rows of every rank's [M, K] buffer (memory shared with CUDA IPC).
+    Two exchanges:
+
+    * ``"stores"`` (default): one kernel, ``rmsnorm_allgather_bf16``, whose
+      threads store each normalised vector into all g buffers, the NVLink
+      traffic spread over the kernel;
+    * ``"copies"``: the RMSNorm into this rank's own buffer, then one
+      ``cudaMemcpyAsync`` per peer on its own stream (copy engines, no SMs).
+
+    Two device flag barriers bracket a call: the first makes sure no rank
+    still reads the buffer (its previous use), the second that every rank's
+    rows have landed.  Run on a second stream, a call overlaps the previous
+    step's GEMM.
 
     Two buffers alternate (``slot``).  Before a call the caller must have
     ordered, on the current stream, every read of that slot's previous
     contents on this rank; the first barrier extends that to all ranks.
     Construction and :meth:`close` are collective; ``peers`` supplies memory,
-    views and the barrier (default: the CUDA library), ``norm`` the per-shard
-    RMSNorm (default: ``bindings.rmsnorm_bf16_into``).  The barriers wait a
-    bounded time; :meth:`check` raises if one gave up.
+    views, the fused RMSNorm and the barrier (default: the CUDA library),
+    ``norm`` the per-shard RMSNorm of the copy exchange (default:
+    ``bindings.rmsnorm_bf16_into``).  The barriers wait a bounded time;
+    :meth:`check` raises if one gave up.
     """
 
     def __init__(self, m: int, k: int, group=None, peers=None,
-                 norm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor, float], None] | None = None
-                 ) -> None:
+                 norm: Callable[[torch.Tensor, torch.Tensor, torch.Tensor, float], None] | None = None,
+                 exchange: str = "stores") -> None:
+        if exchange not in ("stores", "copies"):
+            raise ValueError("exchange must be 'stores' or 'copies'")
+        self.exchange = exchange
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         if not 1 <= self.world <= 8:
@@ -391,10 +405,15 @@ class RowNormGather:
         self.dests = [[self.peers.view(self.addrs[i][j] + row_bytes, self.rows, k)
                        for j in range(self.world)] for i in range(2)]
         self.flag_addrs = [self.addrs[0][j] + self._flag_offset for j in range(self.world)]
+        # where this rank's rows go in buffer i of every rank: its own first,
+        # then rank+1, rank+2, ... (mod g), so that the ranks' first peer
+        # stores go to different GPUs
+        order = [(self.rank + j) % self.world for j in range(self.world)]
+        self.dest_addrs = [[self.addrs[i][r] + row_bytes for r in order] for i in range(2)]
         self.epoch = 0
         self.calls = 0
         self._streams = None
-        if torch.cuda.is_available() and self.outputs[0].is_cuda:
+        if exchange == "copies" and torch.cuda.is_available() and self.outputs[0].is_cuda:
             self._streams = [torch.cuda.Stream() for _ in range(self.world)]
         if self.world > 1:
             dist.barrier(group=group)  # every mapping exists before any copy
@@ -421,6 +440,10 @@ class RowNormGather:
             raise ValueError("slot must be 0 or 1")
         self.calls += 1
         self._barrier()  # nobody still reads buffer i
+        if self.exchange == "stores":
+            self.peers.rmsnorm_gather(x, weight, self.dest_addrs[i], eps)
+            self._barrier()  # every rank's rows have landed
+            return self.outputs[i]
         own = self.outputs[i][lo:lo + self.rows]
         self.norm(x, weight, own, eps)
         if self.world > 1:

@@ -221,6 +221,21 @@ int cuda_operator_gemm_residual_bf16(const void* input_bf16, const void* weight_
  * m == 0 or n == 0 succeeds. */
 int cuda_operator_gemm_swiglu_allgather_bf16(const void* input_bf16, const float* row_scale, const void* packed_weight_bf16, void* const* dests, int num_dests, uint64_t m, uint64_t k, uint64_t n, uint64_t ld, void* stream);
 
+/* Row-sharded bf16 RMSNorm with its row all-gather fused in (no reference
+ * counterpart; the norm of the N-sharded MLP block, whose GEMM on every rank
+ * reads all normalised rows).  Normalises input[rows, cols] with weight[cols]
+ * exactly as cuda_operator_rmsnorm_bf16 does (bit for bit) and stores the
+ * [rows, cols] result into each of the num_dests (1..8) destinations: dests
+ * (a HOST array of device addresses) holds where these rows go in this GPU's
+ * buffer and in the other ranks' buffers as mapped by
+ * cuda_operator_lab_peer_open.  Stores to other GPUs travel over NVLink;
+ * follow the call with cuda_operator_lab_peer_barrier on the same stream
+ * before another rank reads them.  cols must be a multiple of 8 and at most
+ * 8192 and every pointer 16-byte aligned; otherwise, and for NULL pointers,
+ * num_dests outside 1..8 or eps <= 0, cudaErrorInvalidValue; rows == 0
+ * succeeds first. */
+int cuda_operator_rmsnorm_allgather_bf16(const void* input_bf16, const void* weight_bf16, void* const* dests, int num_dests, uint64_t rows, uint64_t cols, float eps, void* stream);
+
 /* Peer memory for the gathering GEMM, shared by the processes of one node
  * (one per GPU) through CUDA IPC.  peer_alloc: zero-filled device allocation
  * of `bytes` on the current device; *ptr = its address, `handle` receives

@@ -18,6 +18,8 @@ from cuda_operator_lab import bindings as b
 def _cpu_args(name: str):
     f32 = lambda *s: torch.zeros(*s, dtype=torch.float32)  # noqa: E731
     bf = lambda *s: torch.zeros(*s, dtype=torch.bfloat16)  # noqa: E731
+    if name == "rmsnorm_allgather_bf16":
+        return [bf(2, 8), bf(8), [1 << 20]]
     if name.startswith("reduction"):
         return [f32(8)]
     if name.startswith("softmax"):

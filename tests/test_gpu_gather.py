@@ -8,9 +8,9 @@ and for a wait that runs out (a flag that nothing sets: the kernel must give
 up after its limit, report it in the peer status word and leave the context
 usable).  With two or more GPUs, ranks in separate processes exchange CUDA
 IPC handles and gather over NVLink through ``sharding.PeerColumnGather``.
-The row-sharded RMSNorm with its copy-engine all-gather
-(``sharding.RowNormGather``) runs as one rank here and across every GPU the
-box has, in both cases bit for bit against the unsharded RMSNorm.
+The row-sharded RMSNorm with its all-gather (``rmsnorm_allgather_bf16`` and
+``sharding.RowNormGather``, peer stores or copy engines) runs as one rank here
+and across every GPU the box has, bit for bit against the unsharded RMSNorm.
 """
 
 from __future__ import annotations
@@ -264,8 +264,44 @@ def _row_norm_case(rng, rank, world, m, k, pipelined):
     return ok
 
 
-def test_row_norm_gather_one_rank():
-    rng = sharding.RowNormGather(384, 4096)
+@pytest.mark.parametrize(("rows", "cols"), [(1, 8), (4, 256), (5, 512), (33, 1024), (9, 2048),
+                                         (300, 2056), (136, 4096), (7, 8192)])
+def test_rmsnorm_allgather_matches_rmsnorm_bit_for_bit(rows, cols):
+    """Every width class of the row engine (8 to 8192 columns): each of three
+    destinations receives exactly what rmsnorm_bf16 writes, and nothing
+    outside its rows (sentinel guard before and after each)."""
+    g = seeded(rows * 31 + cols)
+    x = (torch.randn(rows, cols, generator=g) * 3).to(torch.bfloat16).to(DEV)
+    w = (torch.rand(cols, generator=g) * 2 - 0.5).to(torch.bfloat16).to(DEV)
+    guard = 64
+    bufs = [torch.full((guard + rows * cols + guard,), 0x7FDE, dtype=torch.int16, device=DEV)
+            for _ in range(3)]
+    dests = [buf[guard:].data_ptr() for buf in bufs]
+    b.rmsnorm_allgather_bf16(x, w, dests, 1e-6)
+    expected = b.rmsnorm_bf16(x, w, 1e-6)
+    torch.cuda.synchronize()
+    for buf in bufs:
+        assert torch.equal(buf[guard:guard + rows * cols].view(torch.bfloat16).view(rows, cols),
+                           expected)
+        assert bool((buf[:guard] == 0x7FDE).all()) and bool((buf[guard + rows * cols:] == 0x7FDE).all())
+
+
+def test_rmsnorm_allgather_rejects_what_it_cannot_take():
+    x = torch.zeros(4, 64, dtype=torch.bfloat16, device=DEV)
+    w = torch.ones(64, dtype=torch.bfloat16, device=DEV)
+    out = torch.empty(4 * 64 + 8, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(ValueError):
+        b.rmsnorm_allgather_bf16(x[:, :60].contiguous(), w[:60], [out.data_ptr()], 1e-6)
+    with pytest.raises(ValueError):
+        b.rmsnorm_allgather_bf16(x, w, [out.data_ptr()] * 9, 1e-6)
+    with pytest.raises(RuntimeError, match="CUDA error 1"):  # a destination off 16 bytes
+        b.rmsnorm_allgather_bf16(x, w, [out[1:].data_ptr()], 1e-6)
+    b.rmsnorm_allgather_bf16(x[:0], w, [out.data_ptr()], 1e-6)  # no rows: nothing to do
+
+
+@pytest.mark.parametrize("exchange", ["stores", "copies"])
+def test_row_norm_gather_one_rank(exchange):
+    rng = sharding.RowNormGather(384, 4096, exchange=exchange)
     try:
         assert _row_norm_case(rng, 0, 1, 384, 4096, pipelined=True)
     finally:
@@ -285,9 +321,13 @@ def _row_norm_worker(rank: int, world: int, port: int, results) -> None:
     rng = None
     try:
         m, k = 136 * world, 4096  # 136 rows per rank: not a multiple of a CTA's rows
-        rng = sharding.RowNormGather(m, k)
-        ok = _row_norm_case(rng, rank, world, m, k, pipelined=False)
-        ok = _row_norm_case(rng, rank, world, m, k, pipelined=True) and ok
+        ok = True
+        for exchange in ("stores", "copies"):
+            rng = sharding.RowNormGather(m, k, exchange=exchange)
+            ok = _row_norm_case(rng, rank, world, m, k, pipelined=False) and ok
+            ok = _row_norm_case(rng, rank, world, m, k, pipelined=True) and ok
+            rng.close()
+            rng = None
         results[rank] = (ok, b.peer_status(), b.gemm_status())
     finally:
         if rng is not None:
@@ -297,9 +337,10 @@ def _row_norm_worker(rank: int, world: int, port: int, results) -> None:
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
 def test_row_norm_gather_across_gpus():
-    """Each rank normalises its rows of X and the copy engines place them in
-    every rank's buffer over NVLink: every rank's buffer must equal the
-    unsharded RMSNorm bit for bit after every call."""
+    """Each rank normalises its rows of X and places them in every rank's
+    buffer over NVLink (peer stores from the norm kernel, and copy engines):
+    every rank's buffer must equal the unsharded RMSNorm bit for bit after
+    every call."""
     world = min(torch.cuda.device_count(), 8)
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()

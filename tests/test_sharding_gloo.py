@@ -111,6 +111,7 @@ class HostPeers:
         self.segments: dict[int, shared_memory.SharedMemory] = {}
         self.next = 1
         self.epochs_seen: list[bool] = []
+        self.normed_rows: list[int] = []
 
     def _map(self, shm: shared_memory.SharedMemory) -> int:
         base = self.next << 40
@@ -151,6 +152,15 @@ class HostPeers:
                                     offset=off)
             rows.as_strided((m, n), (ld, 1)).copy_(block)
             del rows
+
+    def rmsnorm_gather(self, x, weight, dests, eps) -> None:
+        """The fused RMSNorm: the oracle's rows written to every destination."""
+        self.normed_rows.append(x.shape[0])
+        rows = oracle.rmsnorm_bf16(x, weight, eps)
+        for d in dests:
+            shm, off = self._resolve(d)
+            torch.frombuffer(shm.buf, dtype=torch.bfloat16, count=rows.numel(),
+                             offset=off).copy_(rows.reshape(-1))
 
     def barrier(self, flag_addrs, rank, epoch) -> None:
         world = len(flag_addrs)
@@ -218,7 +228,7 @@ def test_peer_column_gather_two_gloo_ranks(layout):
     assert dict(results) == {r: (True, True, True, True, True) for r in range(world)}
 
 
-def _row_norm_worker(rank: int, world: int, port: int, results) -> None:
+def _row_norm_worker(rank: int, world: int, port: int, results, exchange: str) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -235,7 +245,7 @@ def _row_norm_worker(rank: int, world: int, port: int, results) -> None:
             out.copy_(oracle.rmsnorm_bf16(x, weight, eps))
 
         peers = HostPeers()
-        rng = sharding.RowNormGather(m, k, peers=peers, norm=norm)
+        rng = sharding.RowNormGather(m, k, peers=peers, norm=norm, exchange=exchange)
         rows = m // world
         ok, ptrs = [], []
         for call, x in enumerate(xs):
@@ -247,7 +257,9 @@ def _row_norm_worker(rank: int, world: int, port: int, results) -> None:
             ptrs.append(out.data_ptr())
             dist.barrier()  # every rank checked before the buffer is reused
         alternate = ptrs[0] == ptrs[2] != ptrs[1]
-        own_rows_only = normed_rows == [rows] * 3
+        own_rows_only = (normed_rows if exchange == "copies" else peers.normed_rows) == [rows] * 3
+        first = rng.dest_addrs[0][0] - rng.addrs[0][rank] == rank * rows * k * 2
+        own_rows_only = own_rows_only and first
         epochs = peers.epochs_seen == [True] * 6 and rng.epoch == 6
         del out
         rng.close()
@@ -256,14 +268,15 @@ def _row_norm_worker(rank: int, world: int, port: int, results) -> None:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["stores", "copies"])
 @pytest.mark.parametrize("world", [2, 4])
-def test_row_norm_gather_gloo_ranks(world):
+def test_row_norm_gather_gloo_ranks(world, exchange):
     """Host logic of the row-sharded RMSNorm with its all-gather: each rank
     normalises only its M/g rows, its rows land in every rank's buffer, two
     barrier epochs per call, alternating buffers, collective close."""
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()
-    mp.start_processes(_row_norm_worker, args=(world, _free_port(), results),
+    mp.start_processes(_row_norm_worker, args=(world, _free_port(), results, exchange),
                        nprocs=world, join=True, start_method="spawn")
     assert dict(results) == {r: (True, True, True, True, True) for r in range(world)}
 
@@ -275,6 +288,8 @@ def test_row_norm_gather_rejects_bad_shapes():
         rng(torch.zeros(4, 8, dtype=torch.bfloat16), torch.zeros(16), 1e-6)
     with pytest.raises(ValueError):
         rng(torch.zeros(8, 16, dtype=torch.bfloat16), torch.zeros(16), 1e-6, slot=2)
+    with pytest.raises(ValueError):
+        sharding.RowNormGather(8, 16, peers=peers, exchange="nccl")
     rng.close()
     assert not peers.segments
 
