@@ -599,10 +599,14 @@ def run_ours(args, d: Dist) -> dict | None:
             rng.check()  # raises if an exchange barrier gave up waiting
             last = rng.outputs[(args.warmup + args.steps - 1) % 2]
             same = torch.equal(last, b.rmsnorm_bf16(x, w_norm, EPS))
+            # the norm and its exchange alone, back to back (no GEMM beside them)
+            alone_ms = time_region(d, lambda: rng(x, w_norm, EPS), args.steps, args.warmup)
+            rng.check()
             sharded_norm = {
                 "identical_to_unsharded": d.max(0.0 if same else 1.0) == 0.0,
                 "rows_per_rank": M // d.world,
                 "nvlink_bytes_per_rank": (d.world - 1) * (M // d.world) * K * 2,
+                "alone_us_per_call": round(1000.0 * alone_ms / args.steps, 1),
                 "exchange": "rmsnorm_allgather_bf16: the norm kernel stores each row into "
                             "every rank's CUDA IPC buffer over NVLink; two device flag "
                             "barriers per step"}
