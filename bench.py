@@ -6,14 +6,14 @@ GEMM+SwiGLU (M=16384, K=4096, N=14336, W[28672, 4096]) -- as GEMM+SwiGLU
 TFLOP/s for the whole job.  One step = the block as the reference defines it:
 the bf16 RMSNorm of all rows (each rank needs the whole normalised X for its N
 slice) writing the normalised X, then the N-sharded GEMM+SwiGLU with bf16
-output.  With N > 1 ranks the RMSNorm is sharded by rows: each rank
-normalises M/N rows and its norm kernel stores them into every rank's X
-buffer over NVLink (peer stores, then a device flag barrier).  Consecutive steps are pipelined over two normalised-X buffers:
-step i's RMSNorm (and exchange) runs on a second stream and overlaps step
-i-1's GEMM.  All inputs
-are resident in HBM (X 134 MB and W 235 MB exceed the 126 MB L2, so no flush
-between steps is needed).  Scaling is strong: the total work is fixed and rank
-r of N owns output columns [r*N/g, (r+1)*N/g).  Inputs are generated on the
+output.  Every rank normalises all rows: sharding the RMSNorm by rows needs
+an NVLink exchange of the normalised rows that measured slower at 2, 4 and 8
+GPUs (reported under ``variants``).  Consecutive steps are pipelined over two
+normalised-X buffers: step i's RMSNorm runs on a second stream and overlaps
+step i-1's GEMM.  All inputs are resident in HBM (X 134 MB and W 235 MB
+exceed the 126 MB L2, so no flush between steps is needed).  Scaling is
+strong: the total work is fixed and rank r of N owns output columns
+[r*N/g, (r+1)*N/g).  Inputs are generated on the
 host from one seed, so the GPU step, the CPU baseline and ``--impl
 reference`` see the same tensors.
 
@@ -21,14 +21,14 @@ Extra keys: ``e2e`` (the same metric through the public API with the X copy
 from pinned host memory -- at N > 1 each rank its own rows -- and the output
 shard copied back inside every step, uploads, compute and downloads of
 consecutive steps overlapped on three streams; ``serial_value`` without the
-overlap), ``sharded_rmsnorm`` (N > 1: the exchanged normalised X checked
-equal to the unsharded RMSNorm), ``roofline`` (the GEMM kernel
-against the measured bf16 peak: burst for a timed region under a second),
+overlap), ``roofline`` (the GEMM kernel against the measured bf16 peak: burst
+for a timed region under a second),
 ``cpu_baseline`` (the CPU oracle, rank 0 at N=1) and ``parity`` (the GPU
 output of the last timed step against that CPU result, every row the CPU
 computed, at the bf16 bar), ``variants`` (the step unpipelined, with the
-RMSNorm folded into the GEMM, and at N > 1 with every rank normalising all
-rows), ``clocks`` (nvidia-smi sampled during the
+RMSNorm folded into the GEMM, and at N > 1 with the RMSNorm sharded by rows
+and its rows exchanged three ways, the exchanged X checked equal to the
+unsharded RMSNorm), ``clocks`` (nvidia-smi sampled during the
 timed region), ``gpu_launches`` and ``ops`` (every other BASELINE config:
 per-op device time, GB/s or TFLOP/s and the fraction of the measured peak,
 timed from CUDA graphs of back-to-back calls -- cold rotates over input sets
@@ -569,50 +569,22 @@ def run_ours(args, d: Dist) -> dict | None:
 
     # One step = the block as the reference defines it: bf16 RMSNorm of every
     # row of X (each rank needs all rows for its N slice) writing normalised X,
-    # then the packed GEMM+SwiGLU of this rank's N slice.  With N ranks the
-    # RMSNorm is sharded by rows: each rank normalises its M/N rows and the
-    # norm kernel stores them into every peer's buffer over NVLink
-    # (sharding.RowNormGather), so no rank repeats the others' work.  Steps
-    # are pipelined over two normalised-X
-    # buffers: step i's RMSNorm (and exchange) runs on a second stream as soon
-    # as the GEMM two steps back has read its buffer -- on every rank, by the
-    # exchange's first barrier -- so it overlaps the previous GEMM; step i's
-    # GEMM waits for it.  Every step's RMSNorm and GEMM run inside the timed
-    # region.  The GEMM's stream has the higher priority: when both kernels
-    # are ready, the block scheduler places the GEMM's CTAs first, and the
-    # RMSNorm's take the SMs that the GEMM's last wave leaves idle.  CUDA
-    # events around every GEMM launch of the timed steps (on the launching
-    # stream) give the dominant kernel's average duration.
+    # then the packed GEMM+SwiGLU of this rank's N slice.  Every rank
+    # normalises all rows: the row-sharded form with its NVLink exchange
+    # (sharding.RowNormGather) gives the same bytes but measured slower at 2,
+    # 4 and 8 GPUs and is timed among the variants.  Steps are pipelined over
+    # two normalised-X buffers: step i's RMSNorm runs on a second stream as
+    # soon as the GEMM two steps back has read its buffer, so it overlaps the
+    # previous GEMM; step i's GEMM waits for it.  Every step's RMSNorm and
+    # GEMM run inside the timed region.  The GEMM's stream has the higher
+    # priority: when both kernels are ready, the block scheduler places the
+    # GEMM's CTAs first.  CUDA events around every GEMM launch of the timed
+    # steps (on the launching stream) give the dominant kernel's average
+    # duration.
     b.gemm_status(clear=True)
-    rng = None
-    if d.world > 1:
-        from cuda_operator_lab import sharding
-
-        rng = sharding.RowNormGather(M, K)
-    try:
-        with ClockSampler(physical_gpus(d.world), enabled=d.rank == 0) as clocks:
-            norm = (lambda j: rng(x, w_norm, EPS, slot=j)) if rng is not None else None
-            ms, gemm_rank_us = pipelined_block(d, args, x, w_norm, packed, out, norm)
-        step_ms_ranks = [v / args.steps for v in d.last_region_ms]
-        sharded_norm = None
-        if rng is not None:
-            rng.check()  # raises if an exchange barrier gave up waiting
-            last = rng.outputs[(args.warmup + args.steps - 1) % 2]
-            same = torch.equal(last, b.rmsnorm_bf16(x, w_norm, EPS))
-            # the norm and its exchange alone, back to back (no GEMM beside them)
-            alone_ms = time_region(d, lambda: rng(x, w_norm, EPS), args.steps, args.warmup)
-            rng.check()
-            sharded_norm = {
-                "identical_to_unsharded": d.max(0.0 if same else 1.0) == 0.0,
-                "rows_per_rank": M // d.world,
-                "nvlink_bytes_per_rank": (d.world - 1) * (M // d.world) * K * 2,
-                "alone_us_per_call": round(1000.0 * alone_ms / args.steps, 1),
-                "exchange": "rmsnorm_allgather_bf16: the norm kernel stores each row into "
-                            "every rank's CUDA IPC buffer over NVLink; two device flag "
-                            "barriers per step"}
-    finally:
-        if rng is not None:
-            rng.close()
+    with ClockSampler(physical_gpus(d.world), enabled=d.rank == 0) as clocks:
+        ms, gemm_rank_us = pipelined_block(d, args, x, w_norm, packed, out, None)
+    step_ms_ranks = [v / args.steps for v in d.last_region_ms]
     gemm_us_ranks = d.values(gemm_rank_us)
     gemm_us = max(gemm_us_ranks)
     clock_info = clocks.summary() if d.rank == 0 else None
@@ -673,13 +645,12 @@ def run_ours(args, d: Dist) -> dict | None:
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) X, N(0,1/K) W, U(0.5,1.5) norm weight)",
         "config": {"workload": "llama_mlp_block (BASELINE config 5)", "M": M, "K": K, "N": N,
-                   "rmsnorm": ("bf16 RMSNorm of all 16384 rows writing the normalised X the "
-                               "GEMM reads (the reference's block semantics); " +
-                               ("sharded by rows: each rank normalises 16384/N rows and its "
-                                "norm kernel stores them into every rank's X buffer over "
-                                "NVLink; " if d.world > 1 else "") +
-                               "step i's RMSNorm on a second stream into one of two X buffers, "
-                               "overlapping step i-1's GEMM"),
+                   "rmsnorm": ("bf16 RMSNorm of all 16384 rows on every rank, writing the "
+                               "normalised X the GEMM reads (the reference's block "
+                               "semantics); step i's RMSNorm on a second stream into one of "
+                               "two X buffers, overlapping step i-1's GEMM" +
+                               ("; the row-sharded form with its NVLink exchange is "
+                                "variants.row_sharded_rmsnorm" if d.world > 1 else "")),
                    "gemm": "packed GEMM+SwiGLU bf16 out, N-sharded",
                    "parallelism": f"N-shard x{d.world}" if d.world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (X 134 MB, W 235 MB); no flush"},
@@ -698,11 +669,9 @@ def run_ours(args, d: Dist) -> dict | None:
                         if d.world > 1 else {})},
         "cpu_baseline": cpu,
         "parity": parity,
-        **({"sharded_rmsnorm": sharded_norm} if sharded_norm is not None else {}),
         "variants": {**variants, **({"gathered_output": gather} if gather is not None else {})},
         "clocks": clock_info,
-        # per step: RMSNorm + GEMM, and at N > 1 the exchange's two barrier kernels
-        "gpu_launches": (2 if d.world == 1 else 4) * args.steps,
+        "gpu_launches": 2 * args.steps,  # per step: RMSNorm + GEMM
         "ops": ops,
     }
 
@@ -789,10 +758,10 @@ def pipelined_block(d: Dist, args, x, w_norm, packed, out, norm=None) -> tuple[f
 def step_variants(d: Dist, args, x, w_norm, packed, out) -> dict:
     """Other forms of the same step, timed in the same run:
 
-    * ``replicated_rmsnorm``, ``nccl_rmsnorm_allgather`` and
-      ``copy_engine_rmsnorm_allgather`` (N > 1): the pipelined step with every
-      rank normalising all rows, or its rows all-gathered by NCCL or by the
-      copy engines, instead of the headline's peer stores from the norm kernel;
+    * ``row_sharded_rmsnorm``, ``nccl_rmsnorm_allgather`` and
+      ``copy_engine_rmsnorm_allgather`` (N > 1): the pipelined step with the
+      RMSNorm sharded by rows, its rows all-gathered by peer stores from the
+      norm kernel, by NCCL or by the copy engines;
     * ``serial``: RMSNorm then GEMM on one stream, one normalised-X buffer
       (no overlap between consecutive steps);
     * ``folded``: the RMSNorm folded into the GEMM (a per-row rstd pass, rstd
@@ -800,7 +769,6 @@ def step_variants(d: Dist, args, x, w_norm, packed, out) -> dict:
       W once).  Its bf16 rounding falls on W * w instead of on the normalised
       X, so it is not the reference's block bit for bit."""
     from cuda_operator_lab import bindings as b
-
     from cuda_operator_lab import sharding
 
     res = {}
@@ -810,13 +778,29 @@ def step_variants(d: Dist, args, x, w_norm, packed, out) -> dict:
                 "ms_per_step": round(ms / args.steps, 4), "step": text}
 
     if d.world > 1:
-        ms, _ = pipelined_block(d, args, x, w_norm, packed, out, None)
-        res["replicated_rmsnorm"] = entry(
-            ms, "pipelined like the headline, every rank normalising all 16384 rows")
         ms, _ = pipelined_block(d, args, x, w_norm, packed, out, norm_nccl(d, x, w_norm))
         res["nccl_rmsnorm_allgather"] = entry(
             ms, "pipelined like the headline, each rank normalising its rows, NCCL "
                 "all_gather_into_tensor of the normalised rows on the second stream")
+        rng = sharding.RowNormGather(M, K)
+        try:
+            ms, _ = pipelined_block(d, args, x, w_norm, packed, out,
+                                    lambda j: rng(x, w_norm, EPS, slot=j))
+            rng.check()  # raises if an exchange barrier gave up waiting
+            last = rng.outputs[(args.warmup + args.steps - 1) % 2]
+            same = torch.equal(last, b.rmsnorm_bf16(x, w_norm, EPS))
+            # the norm and its exchange alone, back to back (no GEMM beside them)
+            alone_ms = time_region(d, lambda: rng(x, w_norm, EPS), args.steps, args.warmup)
+            rng.check()
+        finally:
+            rng.close()
+        res["row_sharded_rmsnorm"] = {
+            **entry(ms, "pipelined like the headline, each rank normalising its 16384/N rows "
+                        "with rmsnorm_allgather_bf16, whose threads store every row into each "
+                        "rank's CUDA IPC buffer over NVLink; two device flag barriers per step"),
+            "identical_to_unsharded": d.max(0.0 if same else 1.0) == 0.0,
+            "nvlink_bytes_per_rank": (d.world - 1) * (M // d.world) * K * 2,
+            "exchange_alone_us_per_call": round(1000.0 * alone_ms / args.steps, 1)}
         rng = sharding.RowNormGather(M, K, exchange="copies")
         try:
             ms, _ = pipelined_block(d, args, x, w_norm, packed, out,
