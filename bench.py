@@ -1,8 +1,9 @@
-"""Benchmark of the sm_100a operator library on BASELINE.json's workloads.
+"""Benchmark of the sm_100a operator library on the operator family's workloads.
 
-Headline (one JSON line on rank 0): the large sharded Llama-style MLP block of
-BASELINE config 5 -- bf16 RMSNorm of x[16384, 4096] feeding the packed
-GEMM+SwiGLU (M=16384, K=4096, N=14336, W[28672, 4096]) -- as GEMM+SwiGLU
+Headline (one JSON line on rank 0): the large sharded Llama-style MLP block
+(configuration 5 of the benchmark set) -- bf16 RMSNorm of x[16384, 4096]
+feeding the packed GEMM+SwiGLU (M=16384, K=4096, N=14336, W[28672, 4096]) --
+as GEMM+SwiGLU
 TFLOP/s for the whole job.  One step = the block as the reference defines it:
 the bf16 RMSNorm of all rows (each rank needs the whole normalised X for its N
 slice) writing the normalised X, then the N-sharded GEMM+SwiGLU with bf16
@@ -29,7 +30,7 @@ computed, at the bf16 bar), ``variants`` (the step unpipelined, with the
 RMSNorm folded into the GEMM, and at N > 1 with the RMSNorm sharded by rows
 and its rows exchanged three ways, the exchanged X checked equal to the
 unsharded RMSNorm), ``clocks`` (nvidia-smi sampled during the
-timed region), ``gpu_launches`` and ``ops`` (every other BASELINE config:
+timed region), ``gpu_launches`` and ``ops`` (every other configuration of the set:
 per-op device time, GB/s or TFLOP/s and the fraction of the measured peak,
 timed from CUDA graphs of back-to-back calls -- cold rotates over input sets
 three times the L2 size, warm repeats one set -- with the CPU oracle's time
@@ -358,7 +359,7 @@ def rotation(make, nbytes: int, min_calls: int = 64) -> tuple[list, list]:
 
 
 def op_table(d: Dist, pk: dict) -> dict:
-    """Every other BASELINE config at N=1 (rank 0), plus the sharded large
+    """Every other benchmark configuration at N=1 (rank 0), plus the sharded large
     RMSNorm and 2^30 reduction at every N.  Single-GPU configs are timed from
     CUDA graphs of back-to-back calls: cold rotates over input sets 3x the
     L2 size, warm repeats one set."""
