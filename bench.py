@@ -117,9 +117,11 @@ class Dist:
             # and its set-up lines precede the run; then a summary of this rank
             t = torch.ones(1, device="cuda")
             dist.all_reduce(t)
-            print(f"[bench] rank {self.rank}/{self.world}: NCCL communicator of "
-                  f"{int(t.item())} ranks on cuda:{self.local_rank} "
-                  f"({torch.cuda.get_device_name(self.local_rank)})", file=sys.stderr, flush=True)
+            # one write per line: the ranks share the stream
+            sys.stderr.write(f"[bench] rank {self.rank}/{self.world}: NCCL communicator of "
+                             f"{int(t.item())} ranks on cuda:{self.local_rank} "
+                             f"({torch.cuda.get_device_name(self.local_rank)})\n")
+            sys.stderr.flush()
         elif torch.cuda.is_available():
             torch.cuda.set_device(0)
 
